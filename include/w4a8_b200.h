@@ -1,0 +1,136 @@
+/*
+ * w4a8_b200.h -- C ABI of libw4a8_b200.so, the B200 (sm_100a) mid-group W4A8
+ * linear layer.
+ *
+ * All tensor arguments are raw device pointers to densely packed row-major
+ * arrays; bf16 values are 16-bit patterns.  `stream` is a cudaStream_t (NULL =
+ * legacy default stream).  Every call is asynchronous on `stream`, allocates
+ * no memory, and returns W4A8_OK or a negative status.  Asynchronous failures
+ * inside a kernel (a pipeline wait that ran out) are recorded in the
+ * workspace's status word: read it with w4a8_workspace_status().
+ *
+ * Layout conventions (the reference's; mg_kgeom.h in the reference project):
+ *   G    = ceil(K / group_size)                       -- w4a8_num_groups()
+ *   Kpad = group-padded row length (each group padded to 64 elements;
+ *          only the last group can pad when group_size % 64 == 0)
+ *   packed int4 weights: [N, Kpad/2] bytes, two codes per byte, even k in the
+ *          low nibble, codes in [-8, 7]
+ *   scales / zero points: group-major [G, N] (weights), [G, M] (activations)
+ *   zero points: integers in code units held in bf16 (asymmetric weights)
+ *
+ * Each entry point cites the reference interface it replaces.
+ */
+#ifndef W4A8_B200_H
+#define W4A8_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define W4A8_API __attribute__((visibility("default")))
+#else
+#define W4A8_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W4A8_OK 0
+#define W4A8_ERR_INVALID (-1)     /* bad shape, null or misaligned pointer       */
+#define W4A8_ERR_UNSUPPORTED (-2) /* group size / dtype not built                */
+#define W4A8_ERR_CUDA (-3)        /* a CUDA call failed: w4a8_last_cuda_error()  */
+#define W4A8_ERR_WORKSPACE (-4)   /* workspace missing or smaller than required  */
+#define W4A8_ERR_DEVICE (-5)      /* current device is not an sm_100 part         */
+
+#define W4A8_DTYPE_BF16 0
+#define W4A8_DTYPE_F32 1
+
+/* ---- geometry (npu_ops/python/w4a8_ops.py:63-82,160-178; mg_kgeom.h:64-101) ---- */
+W4A8_API int64_t w4a8_num_groups(int64_t K, int32_t group_size);
+W4A8_API int64_t w4a8_k_pad_elems(int64_t K, int32_t group_size);
+/* Rows `midgroup_quant_a` emits for M rows: M rounded up to 16 / 64 / 128
+ * (TileMFor, npu_ops/host/midgroup_quant_a.cpp:37). */
+W4A8_API int64_t w4a8_pad_rows(int64_t M);
+
+/* ---- fused linear: y = x @ W^T, activation quantised per (token, group) ----
+ * Replaces MidGroupW4A8LinearMethod.apply's quant_a -> gemm pair
+ * (npu_ops/python/midgroup_quant.py:163-178, w4a8_ops.py:243-252).
+ *   x        bf16 [M, ldx] (ldx >= K)
+ *   w_packed int8 [N, Kpad/2]            (16-byte aligned)
+ *   w_scale  [G, N] bf16 or f32 (w_scale_dtype)
+ *   w_zero   [G, N] bf16, or NULL for symmetric weights
+ *   y        bf16 [M, ldy] (ldy >= N)
+ * group_size in {64, 128, 256, 1024}; N % 8 == 0.
+ * The workspace (w4a8_linear_workspace_size bytes, 1024-byte aligned) must be
+ * zero-filled before its first use; calls leave it reusable.  Calls that share
+ * a workspace must not overlap in time (use one workspace per stream). */
+W4A8_API size_t w4a8_linear_workspace_size(int64_t M, int64_t N, int64_t K, int32_t group_size);
+W4A8_API int w4a8_linear(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t group_size,
+                const void* w_packed, const void* w_scale, int32_t w_scale_dtype,
+                const void* w_zero, void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+/* The two halves of w4a8_linear, for callers that quantise once and reuse the
+ * quantised activation, or time the GEMM alone.  w4a8_linear_gemm reads the
+ * activation w4a8_linear_quant left in the same workspace (same M, K). */
+W4A8_API int w4a8_linear_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N,
+                      int32_t group_size, void* workspace, size_t workspace_bytes, void* stream);
+W4A8_API int w4a8_linear_gemm(int64_t M, int64_t K, int64_t N, int32_t group_size, const void* w_packed,
+                     const void* w_scale, int32_t w_scale_dtype, const void* w_zero, void* y,
+                     int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- activation quantiser (fakequant_lab/quant.py:89-141 semantics) ----
+ *   a_q       int8 [M, K] natural order
+ *   a_scale   [G, M] bf16 bits or f32 (scale_dtype)
+ *   a_ksum    int32 [G, M] NEGATED per-group code sums, or NULL */
+W4A8_API int w4a8_quant_act(const void* x, int64_t M, int64_t K, int64_t ldx, int32_t group_size,
+                   int8_t* a_q, void* a_scale, int32_t scale_dtype, int32_t* a_ksum, void* stream);
+
+/* ---- the reference op torch.ops.npu.midgroup_quant_a ----
+ * (npu_ops/host/midgroup_quant_a.cpp:40-78; schema :87-90).  Emits Mp rows
+ * (Mp >= M; rows [M, Mp) encode zero with scale = bf16 tiny):
+ *   a_hi, a_lo int8 [Mp, Kpad/2]   MSD int4 planes: q = 16*hi + lo + 8
+ *   a_scale    bf16 [G, Mp]
+ *   a_ksum     int32 [G, Mp]       negated code sums */
+W4A8_API int w4a8_midgroup_quant_a(const void* x, int64_t M, int64_t K, int32_t group_size, int64_t Mp,
+                          int8_t* a_hi, int8_t* a_lo, void* a_scale, int32_t* a_ksum, void* stream);
+
+/* ---- the reference op torch.ops.npu.midgroup_w4a8_gemm ----
+ * (npu_ops/host/midgroup_w4a8_gemm.cpp:143-238; schema :249-250).  Computes the
+ * definition form y = sum_g as*ws*sum_k A*(W - wz) from the MSD planes
+ * (ReferenceMidGroupGemm, int4_cube_lab/host/gemm_ref.cpp:199-240); a_ksum and
+ * w_ksum are the MSD bookkeeping of the reference kernel and are not needed by
+ * this path (they may be NULL).  M = rows of a_hi; y bf16 [M, N].
+ * Workspace: w4a8_midgroup_gemm_workspace_size bytes, zero-filled before first use. */
+W4A8_API size_t w4a8_midgroup_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int32_t group_size);
+W4A8_API int w4a8_midgroup_w4a8_gemm(const int8_t* a_hi, const int8_t* a_lo, const void* a_scale,
+                            const int32_t* a_ksum, int64_t M, const int8_t* w_q,
+                            const void* w_scale, const int32_t* w_ksum, const void* w_zero,
+                            int64_t N, int64_t K, int32_t group_size, void* y, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* ---- int32 per-group partials P[g, m, n] = sum_{k in g} A_q*(W - wz) ----
+ * The exactness contract of the reference (fakequant_lab/run_selftest.py:104-141,
+ * int4_cube_lab/host/ragged_layout_test.cpp:112-148), computed by the same
+ * tensor-core path as w4a8_linear.  partials int32 [G, M, N].  Test-sized
+ * problems; workspace as for w4a8_linear. */
+W4A8_API int w4a8_group_partials(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N,
+                        int32_t group_size, const void* w_packed, const void* w_zero,
+                        int32_t* partials, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- status ---- */
+/* Synchronises `stream` and returns the device status word of `workspace`
+ * (0 = no kernel reported a failure; otherwise 0x100 + the id of the wait
+ * that ran out).  reset != 0 clears it. */
+W4A8_API int w4a8_workspace_status(void* workspace, int32_t reset, void* stream);
+W4A8_API const char* w4a8_status_string(int status);
+W4A8_API int w4a8_last_cuda_error(void);
+/* Library build: returns the sm architecture it was compiled for (100). */
+W4A8_API int w4a8_build_arch(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W4A8_B200_H */

@@ -1,0 +1,264 @@
+"""GPU parity: the sm_100a kernels against the CPU oracle on the same seeded
+inputs.  Integer work (codes, MSD planes, int32 group partials) must be
+bit-exact; bf16 outputs must satisfy the stated tolerance:
+
+    max|y - ref| / max|ref| <= 1e-2   and   cosine(y, ref) >= 0.9999
+
+against the float64 exact-integer reference (``oracle.gemm_f64``), and be
+within a few bf16 ulps of the oracle's fp32 kernel-order result."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+MAX_REL = 1e-2
+MIN_COS = 0.9999
+
+
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def _bf16_cuda(bits: np.ndarray):
+    return torch.from_numpy(np.ascontiguousarray(bits, np.uint16).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def _bits(t) -> np.ndarray:
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _weights(w, gk, dev, scale_dtype=torch.float32):
+    from w4a8_b200 import ops
+    codes = torch.from_numpy(w.codes)
+    packed = ops.pack_int4_grouped(codes, gk).to(dev)
+    ws = torch.from_numpy(w.scale).to(dev, scale_dtype)
+    wz = None if w.zero is None else torch.from_numpy(w.zero).to(torch.bfloat16).to(dev)
+    return packed, ws, wz
+
+
+def _close(y, ref64, yk=None):
+    y = np.asarray(y, np.float64)
+    err = np.abs(y - ref64).max() / max(np.abs(ref64).max(), 1e-30)
+    cos = float((y * ref64).sum() / (np.linalg.norm(y) * np.linalg.norm(ref64) + 1e-300))
+    assert err <= MAX_REL, f"max rel {err}"
+    assert cos >= MIN_COS, f"cosine {cos}"
+    if yk is not None:
+        # y differs from the oracle's fp32 kernel-order result only in fp32
+        # accumulation order before the bf16 rounding: at most 2 bf16 ulps.
+        yk = yk.astype(np.float64)
+        d = np.abs(y - yk)
+        tol = 2 * 2.0 ** -7 * np.abs(yk) + 1e-6 * np.abs(yk).max()
+        assert np.all(d <= tol), f"worst {np.max(d / tol)} of the 2-ulp bound"
+
+
+# ------------------------------------------------------------------ quantiser
+
+QUANT_SHAPES = [(1, 128, 128), (4, 1024, 128), (3, 512, 64), (2, 2048, 1024), (5, 768, 256),
+                (7, 1057, 1024), (3, 777, 128), (2, 33, 64), (16, 5120, 128), (1, 27648, 128),
+                (130, 640, 64)]
+
+
+@pytest.mark.parametrize("M,K,gk", QUANT_SHAPES)
+def test_quant_act_bitexact(orc, M, K, gk):
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    _dev()
+    xb = syn.activation_np(M, K, 1000 + M + K)
+    q, s, ks = ops.quant_act(_bf16_cuda(xb), gk)
+    oq, os_, oks = orc.quant_act(xb, gk)
+    assert np.array_equal(q.cpu().numpy(), oq)
+    assert np.array_equal(_bits(s), os_)
+    assert np.array_equal(ks.cpu().numpy(), oks)
+
+
+def test_quant_act_golden(golden):
+    from w4a8_b200 import ops
+    _dev()
+    for p in ["q0_", "q1_", "q2_", "q3_", "q4_", "qr_"]:
+        q, s, _ = ops.quant_act(_bf16_cuda(golden[p + "x"]), int(golden[p + "gk"]))
+        assert np.array_equal(q.cpu().numpy(), golden[p + "q"]), p
+        assert np.array_equal(_bits(s).T, golden[p + "scale"]), p
+
+
+def test_quant_act_f32_scale(orc):
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    _dev()
+    xb = syn.activation_np(9, 1280, 77)
+    q, s, _ = ops.quant_act(_bf16_cuda(xb), 128, scale_dtype=torch.float32, with_ksum=False)
+    oq, os_, _ = orc.quant_act(xb, 128)
+    assert np.array_equal(q.cpu().numpy(), oq)
+    assert np.array_equal(s.cpu().numpy(), orc.bf16_to_f32(os_))
+
+
+@pytest.mark.parametrize("M,K,gk", [(1, 5120, 1024), (16, 5120, 128), (17, 1057, 1024), (64, 640, 64),
+                                    (65, 777, 256), (130, 2048, 128)])
+def test_midgroup_quant_a_bitexact(orc, M, K, gk):
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    _dev()
+    xb = syn.activation_np(M, K, 2000 + M)
+    hi, lo, s, ks = ops.midgroup_quant_a(_bf16_cuda(xb), gk)
+    Mp = ops.pad_rows(M)
+    ohi, olo, os_, oks = orc.midgroup_quant_a(xb, Mp, gk)
+    assert hi.shape == (Mp, ohi.shape[1])
+    assert np.array_equal(hi.cpu().numpy(), ohi)
+    assert np.array_equal(lo.cpu().numpy(), olo)
+    assert np.array_equal(_bits(s), os_)
+    assert np.array_equal(ks.cpu().numpy(), oks)
+
+
+# ------------------------------------------------------------------ group partials (bit-exact)
+
+PARTIAL_CASES = [  # M, N, K, gk, asym
+    (1, 128, 256, 128, False), (16, 256, 1024, 128, False), (16, 256, 1024, 128, True),
+    (5, 128, 640, 64, False), (7, 256, 1280, 256, True), (3, 128, 2048, 1024, True),
+    (3, 128, 2048, 1024, False), (33, 384, 768, 128, False), (64, 128, 512, 64, True),
+    (100, 256, 1024, 256, False), (200, 256, 640, 128, True), (3, 128, 1057, 1024, True),
+    (2, 128, 777, 128, False), (4, 128, 3456, 128, True), (1, 1024, 5120, 128, False),
+]
+
+
+@pytest.mark.parametrize("M,N,K,gk,asym", PARTIAL_CASES)
+def test_group_partials_bitexact(orc, M, N, K, gk, asym):
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    xb = syn.activation_np(M, K, 3000 + M + K)
+    w = syn.weight_np(N, K, gk, 4000 + N + K, asym=asym)
+    packed, _, wz = _weights(w, gk, dev)
+    P = ops.group_partials(_bf16_cuda(xb), packed, wz, gk).cpu().numpy()
+    q, _, _ = orc.quant_act(xb, gk)
+    ref = orc.group_partials(q, w.codes, w.zero, gk)
+    assert np.array_equal(P, ref), f"{np.sum(P != ref)} of {P.size} partials differ"
+    assert ops.workspace_status() == 0
+
+
+def test_group_partials_golden(golden):
+    """Against the int64 partials of the reference's own T4 reference."""
+    from w4a8_b200 import ops
+    dev = _dev()
+    for i in range(5):
+        p = f"g{i}_"
+        M, N, K, gk, asym, sbf = (int(v) for v in golden[p + "meta"])
+        packed = ops.pack_int4_grouped(torch.from_numpy(golden[p + "codes"]), gk).to(dev)
+        wz = torch.from_numpy(golden[p + "wz"]).to(torch.bfloat16).to(dev) if asym else None
+        P = ops.group_partials(_bf16_cuda(golden[p + "x"]), packed, wz, gk).cpu().numpy()
+        assert np.array_equal(P, golden[p + "P"]), p
+
+
+# ------------------------------------------------------------------ fused linear (tolerance)
+
+LINEAR_CASES = [  # M, N, K, gk, asym, scale_dtype
+    (1, 128, 256, 128, False, "f32"), (16, 512, 1024, 128, False, "f32"), (16, 512, 1024, 128, True, "bf16"),
+    (9, 256, 640, 64, False, "bf16"), (31, 256, 1280, 256, True, "f32"), (48, 128, 2048, 1024, True, "bf16"),
+    (64, 384, 1024, 128, False, "f32"), (65, 256, 1024, 128, True, "f32"), (256, 512, 1024, 128, False, "bf16"),
+    (300, 256, 1057, 1024, False, "f32"), (4, 128, 3456, 128, True, "bf16"), (128, 896, 640, 128, False, "f32"),
+]
+
+
+@pytest.mark.parametrize("M,N,K,gk,asym,sd", LINEAR_CASES)
+def test_linear_tolerance(orc, M, N, K, gk, asym, sd):
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    xb = syn.activation_np(M, K, 5000 + M + K)
+    w = syn.weight_np(N, K, gk, 6000 + N + K, asym=asym, scale_bf16=(sd == "bf16"))
+    packed, ws, wz = _weights(w, gk, dev, torch.bfloat16 if sd == "bf16" else torch.float32)
+    y = ops.linear(_bf16_cuda(xb), packed, ws, wz, gk)
+    yf = orc.bf16_to_f32(_bits(y))
+    y64, _ = orc.linear(xb, w.codes, w.scale, w.zero, gk, exact=True)
+    yk, _ = orc.linear(xb, w.codes, w.scale, w.zero, gk)
+    _close(yf, y64, orc.bf16_to_f32(orc.f32_to_bf16(yk)))
+    assert ops.workspace_status() == 0
+
+
+def test_linear_golden(golden, orc):
+    """Against FakeQuantLinear._kernel_gemm output stored by make_golden.py."""
+    from w4a8_b200 import ops
+    dev = _dev()
+    for i in range(5):
+        p = f"g{i}_"
+        M, N, K, gk, asym, sbf = (int(v) for v in golden[p + "meta"])
+        packed = ops.pack_int4_grouped(torch.from_numpy(golden[p + "codes"]), gk).to(dev)
+        ws = torch.from_numpy(golden[p + "ws"]).to(dev)
+        wz = torch.from_numpy(golden[p + "wz"]).to(torch.bfloat16).to(dev) if asym else None
+        y = ops.linear(_bf16_cuda(golden[p + "x"]), packed, ws, wz, gk)
+        _close(orc.bf16_to_f32(_bits(y)), golden[p + "y64"])
+
+
+def test_linear_deterministic_and_repeatable(orc):
+    """Stream-K reduction order is fixed: repeated calls give identical bits."""
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    M, N, K, gk = 16, 1024, 5120, 128
+    xb = syn.activation_np(M, K, 7)
+    w = syn.weight_np(N, K, gk, 8)
+    packed, ws, _ = _weights(w, gk, dev)
+    x = _bf16_cuda(xb)
+    ys = [_bits(ops.linear(x, packed, ws, None, gk)) for _ in range(3)]
+    assert all(np.array_equal(ys[0], y) for y in ys[1:])
+
+
+def test_config0_full_size(orc):
+    """M=16 K=5120 N=7168 GK=128, fp32 lognormal scales."""
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    M, K, N, gk = 16, 5120, 7168, 128
+    xb = syn.activation_np(M, K, 0)
+    w = syn.weight_np(N, K, gk, 1)
+    packed, ws, _ = _weights(w, gk, dev)
+    x = _bf16_cuda(xb)
+    P = ops.group_partials(x, packed, None, gk).cpu().numpy()
+    q, _, _ = orc.quant_act(xb, gk)
+    assert np.array_equal(P, orc.group_partials(q, w.codes, None, gk))
+    y = ops.linear(x, packed, ws, None, gk)
+    y64, _ = orc.linear(xb, w.codes, w.scale, None, gk, exact=True)
+    _close(orc.bf16_to_f32(_bits(y)), y64)
+
+
+# ------------------------------------------------------------------ reference-compatible GEMM
+
+@pytest.mark.parametrize("M,N,K,gk", [(1, 128, 1024, 1024), (16, 256, 5120, 1024), (20, 128, 1057, 1024),
+                                      (64, 256, 1280, 128), (130, 128, 2048, 256)])
+def test_midgroup_gemm_compat(orc, M, N, K, gk):
+    """quant_a -> gemm, the reference op pair, against ReferenceMidGroupGemm semantics."""
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    xb = syn.activation_np(M, K, 9000 + M)
+    w = syn.weight_np(N, K, gk, 9100 + N, asym=True, scale_bf16=True)
+    packed, ws, wz = _weights(w, gk, dev, torch.bfloat16)
+    a_hi, a_lo, a_s, a_k = ops.midgroup_quant_a(_bf16_cuda(xb), gk)
+    y = ops.midgroup_w4a8_gemm(a_hi, a_lo, a_s, a_k, packed, ws, None, wz, K, gk)
+    assert y.shape == (ops.pad_rows(M), N)
+    y = y[:M]
+    y64, _ = orc.linear(xb, w.codes, w.scale, w.zero, gk, exact=True)
+    _close(orc.bf16_to_f32(_bits(y)), y64)
+    if orc.ref_available():
+        q, s, _ = orc.quant_act(xb, gk)
+        yref = orc.ref_midgroup_gemm(q, s, w.codes, orc.f32_to_bf16(w.scale), orc.f32_to_bf16(w.zero), gk)
+        d = np.abs(orc.bf16_to_f32(_bits(y)).astype(np.float64) - orc.bf16_to_f32(yref))
+        assert d.max() <= 2 * 2.0 ** -7 * np.abs(orc.bf16_to_f32(yref)).max()
+
+
+def test_errors_raise():
+    from w4a8_b200 import ops
+    dev = _dev()
+    x = torch.zeros(4, 256, dtype=torch.bfloat16, device=dev)
+    w = torch.zeros(128, 128, dtype=torch.int8, device=dev)
+    s = torch.zeros(2, 128, dtype=torch.float32, device=dev)
+    with pytest.raises(RuntimeError):
+        ops.linear(x.float(), w, s, None, 128)                      # dtype
+    with pytest.raises(RuntimeError):
+        ops.linear(x, w[:, :64], s, None, 128)                      # packed row length
+    with pytest.raises(RuntimeError):
+        ops.linear(x, w, s, None, 96)                               # unsupported group size
+    y = ops.linear(x, w, s, None, 128)
+    assert torch.count_nonzero(y) == 0

@@ -1,0 +1,440 @@
+// w4a8_capi.cu -- the C ABI of libw4a8_b200.so (declared in include/w4a8_b200.h).
+//
+// Host-side work only: argument checks (the reference's TORCH_CHECKs,
+// npu_ops/host/midgroup_w4a8_gemm.cpp:149-183), workspace carving, TMA
+// descriptor encoding, tile / grid sizing, and the two launches of a linear
+// call (quantiser, then the GEMM with programmatic dependent launch so its
+// weight stream starts while the quantiser is still running).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "w4a8_b200.h"
+#include "w4a8_kernels.h"
+
+using namespace w4a8;
+
+namespace {
+
+thread_local int g_last_cuda = 0;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+constexpr int kMaxDev = 64;
+int g_sms[kMaxDev] = {0};
+int g_major[kMaxDev] = {0};
+
+int fail_cuda(cudaError_t e)
+{
+    g_last_cuda = static_cast<int>(e);
+    return W4A8_ERR_CUDA;
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+bool group_ok(int32_t gk) { return gk == 64 || gk == 128 || gk == 256 || gk == 1024; }
+
+int64_t kpad_of(int64_t K, int32_t gk)
+{
+    const int64_t G = cdiv(K, gk);
+    const int64_t stride = round_up(gk, 64);
+    const int64_t last = K - (G - 1) * gk;
+    return (G - 1) * stride + round_up(last, 64);
+}
+
+int device_info(int* sms)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_cuda(e);
+    if (dev < 0 || dev >= kMaxDev) return W4A8_ERR_DEVICE;
+    if (g_sms[dev] == 0) {
+        int n = 0, major = 0;
+        if ((e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return fail_cuda(e);
+        if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess) return fail_cuda(e);
+        g_major[dev] = major;
+        g_sms[dev] = n;
+    }
+    if (g_major[dev] != 10) return W4A8_ERR_DEVICE;
+    *sms = g_sms[dev];
+    return W4A8_OK;
+}
+
+int get_encoder()
+{
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode ? W4A8_OK : W4A8_ERR_CUDA;
+}
+
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw)
+{
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = g_encode(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Per-call geometry and the workspace carve-up.
+struct Plan {
+    int64_t M, N, K, Kpad, G;
+    int gk, tt, n_wt, n_tt, upt, units, grid, kb_total, as_ld;
+    size_t off_counters, off_as, off_aq, off_part, total;
+};
+
+Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
+{
+    Plan p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.gk = gk;
+    p.G = cdiv(K, gk);
+    p.Kpad = kpad_of(K, gk);
+    p.tt = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
+    p.n_wt = static_cast<int>(cdiv(N, 128));
+    p.n_tt = static_cast<int>(cdiv(M, p.tt));
+    p.kb_total = static_cast<int>(cdiv(p.Kpad, 256));
+    p.upt = gk <= 256 ? p.kb_total : static_cast<int>(p.G);
+    p.units = p.n_wt * p.n_tt * p.upt;
+    p.grid = std::max(1, std::min(sms, p.units));
+    p.as_ld = static_cast<int>(round_up(M, 4));
+    size_t off = 256;                                                     // status word block
+    p.off_counters = off;
+    off += round_up(static_cast<int64_t>(p.n_wt) * p.n_tt * 4, 256);
+    off = round_up(off, 1024);
+    p.off_as = off;
+    off += round_up(p.G * p.as_ld * 4, 1024);
+    p.off_aq = off;
+    off += round_up(M * p.Kpad, 1024);
+    p.off_part = off;
+    off += static_cast<size_t>(2) * p.grid * p.tt * 128 * 4;
+    p.total = round_up(off, 1024);
+    return p;
+}
+
+bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }
+
+int check_common(int64_t M, int64_t N, int64_t K, int32_t gk)
+{
+    if (M < 0 || N <= 0 || K <= 0) return W4A8_ERR_INVALID;
+    if (!group_ok(gk)) return W4A8_ERR_UNSUPPORTED;
+    if (N % 8 != 0) return W4A8_ERR_INVALID;
+    if (M > (int64_t(1) << 30) || K > (int64_t(1) << 30) || N > (int64_t(1) << 30)) return W4A8_ERR_INVALID;
+    return W4A8_OK;
+}
+
+// Quantise x into the GEMM's operand order inside the workspace.
+int run_quant_kernel_layout(const Plan& pl, const void* x, int64_t ldx, uint8_t* ws, cudaStream_t st)
+{
+    QuantParams q{};
+    q.x = static_cast<const uint16_t*>(x);
+    q.ldx = ldx;
+    q.M = static_cast<int>(pl.M);
+    q.K = static_cast<int>(pl.K);
+    q.Kpad = static_cast<int>(pl.Kpad);
+    q.G = static_cast<int>(pl.G);
+    q.gk = pl.gk;
+    q.rows = static_cast<int>(pl.M);
+    q.vec_ok = aligned(x, 16) && (pl.K % 8 == 0) && (ldx % 8 == 0);
+    q.aq = reinterpret_cast<int8_t*>(ws + pl.off_aq);
+    q.as = reinterpret_cast<float*>(ws + pl.off_as);
+    q.as_ld = pl.as_ld;
+    const cudaError_t e = launch_quant_act(q, kOutKernel, st, true);
+    return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
+}
+
+int run_gemm(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
+             void* out, int64_t ldy, bool partials, uint8_t* ws, cudaStream_t st)
+{
+    if (get_encoder() != W4A8_OK) return fail_cuda(cudaErrorNotSupported);
+    GemmParams g;
+    std::memset(&g, 0, sizeof(g));
+    const int gpk = pl.gk <= 256 ? 256 / pl.gk : 1;
+    const bool ok =
+        encode_2d(&g.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_packed, pl.Kpad / 2, pl.N, pl.Kpad / 2, 128, 128,
+                  CU_TENSOR_MAP_SWIZZLE_128B) &&
+        encode_2d(&g.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, ws + pl.off_aq, pl.Kpad, pl.M, pl.Kpad, 128, pl.tt,
+                  CU_TENSOR_MAP_SWIZZLE_128B) &&
+        (partials
+             // scales are not read in this mode: describe a small region the workspace owns
+             ? encode_2d(&g.tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.as_ld, pl.G, pl.as_ld * 4,
+                         128, gpk, CU_TENSOR_MAP_SWIZZLE_NONE)
+             : encode_2d(&g.tm_ws,
+                         ws_dtype == W4A8_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                         w_scale, pl.N, pl.G, pl.N * (ws_dtype == W4A8_DTYPE_F32 ? 4 : 2), 128, gpk,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) &&
+        (w_zero == nullptr ||
+         encode_2d(&g.tm_wz, CU_TENSOR_MAP_DATA_TYPE_UINT16, w_zero, pl.N, pl.G, pl.N * 2, 128, gpk,
+                   CU_TENSOR_MAP_SWIZZLE_NONE)) &&
+        encode_2d(&g.tm_as, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.M, pl.G, pl.as_ld * 4, pl.tt, gpk,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!ok) return W4A8_ERR_INVALID;
+    g.out = out;
+    g.partials = reinterpret_cast<float*>(ws + pl.off_part);
+    g.counters = reinterpret_cast<int*>(ws + pl.off_counters);
+    g.status = reinterpret_cast<int*>(ws);
+    g.M = static_cast<int>(pl.M);
+    g.N = static_cast<int>(pl.N);
+    g.Kpad = static_cast<int>(pl.Kpad);
+    g.G = static_cast<int>(pl.G);
+    g.ldy = ldy;
+    g.n_wt = pl.n_wt;
+    g.n_tt = pl.n_tt;
+    g.units_per_tile = pl.upt;
+    g.total_units = pl.units;
+    g.kb_total = pl.kb_total;
+    GemmConfig c{};
+    c.tt = pl.tt;
+    c.gk = pl.gk;
+    c.asym = w_zero != nullptr;
+    c.ws_bf16 = ws_dtype != W4A8_DTYPE_F32;
+    c.partials = partials;
+    const cudaError_t e = launch_gemm(g, c, pl.grid, st, true);
+    return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
+}
+
+int check_weights(const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero)
+{
+    if (!w_packed || !w_scale) return W4A8_ERR_INVALID;
+    if (ws_dtype != W4A8_DTYPE_BF16 && ws_dtype != W4A8_DTYPE_F32) return W4A8_ERR_UNSUPPORTED;
+    if (!aligned(w_packed, 16) || !aligned(w_scale, 16) || (w_zero && !aligned(w_zero, 16))) return W4A8_ERR_INVALID;
+    return W4A8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t w4a8_num_groups(int64_t K, int32_t gk) { return (K <= 0 || gk <= 0) ? 0 : cdiv(K, gk); }
+
+int64_t w4a8_k_pad_elems(int64_t K, int32_t gk) { return (K <= 0 || gk <= 0) ? 0 : kpad_of(K, gk); }
+
+int64_t w4a8_pad_rows(int64_t M)
+{
+    const int64_t t = M <= 16 ? 16 : (M <= 64 ? 64 : 128);
+    return round_up(M, t);
+}
+
+size_t w4a8_linear_workspace_size(int64_t M, int64_t N, int64_t K, int32_t gk)
+{
+    if (check_common(M, N, K, gk) != W4A8_OK) return 0;
+    int sms = 0;
+    if (device_info(&sms) != W4A8_OK) sms = 148;
+    return make_plan(std::max<int64_t>(M, 1), N, K, gk, sms).total;
+}
+
+size_t w4a8_midgroup_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int32_t gk)
+{
+    return w4a8_linear_workspace_size(M, N, K, gk);
+}
+
+int w4a8_linear_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk, void* workspace,
+                      size_t workspace_bytes, void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < K || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    return run_quant_kernel_layout(pl, x, ldx, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+int w4a8_linear_gemm(int64_t M, int64_t K, int64_t N, int32_t gk, const void* w_packed, const void* w_scale,
+                     int32_t ws_dtype, const void* w_zero, void* y, int64_t ldy, void* workspace,
+                     size_t workspace_bytes, void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if ((rc = check_weights(w_packed, w_scale, ws_dtype, w_zero)) != W4A8_OK) return rc;
+    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    return run_gemm(pl, w_packed, w_scale, ws_dtype, w_zero, y, ldy, false, static_cast<uint8_t*>(workspace),
+                    static_cast<cudaStream_t>(stream));
+}
+
+int w4a8_linear(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk, const void* w_packed,
+                const void* w_scale, int32_t ws_dtype, const void* w_zero, void* y, int64_t ldy, void* workspace,
+                size_t workspace_bytes, void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < K || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if ((rc = check_weights(w_packed, w_scale, ws_dtype, w_zero)) != W4A8_OK) return rc;
+    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
+    return run_gemm(pl, w_packed, w_scale, ws_dtype, w_zero, y, ldy, false, ws, st);
+}
+
+int w4a8_group_partials(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
+                        const void* w_packed, const void* w_zero, int32_t* partials, void* workspace,
+                        size_t workspace_bytes, void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < K || !aligned(x, 2) || !partials) return W4A8_ERR_INVALID;
+    if (!w_packed || !aligned(w_packed, 16) || (w_zero && !aligned(w_zero, 16))) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
+    return run_gemm(pl, w_packed, ws + pl.off_as, W4A8_DTYPE_F32, w_zero, partials, N, true, ws, st);
+}
+
+int w4a8_quant_act(const void* x, int64_t M, int64_t K, int64_t ldx, int32_t gk, int8_t* a_q, void* a_scale,
+                   int32_t scale_dtype, int32_t* a_ksum, void* stream)
+{
+    if (M < 0 || K <= 0 || !group_ok(gk)) return M < 0 || K <= 0 ? W4A8_ERR_INVALID : W4A8_ERR_UNSUPPORTED;
+    if (M == 0) return W4A8_OK;
+    if (!x || !a_q || !a_scale || ldx < K || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if (scale_dtype != W4A8_DTYPE_BF16 && scale_dtype != W4A8_DTYPE_F32) return W4A8_ERR_UNSUPPORTED;
+    int sms = 0;
+    int rc = device_info(&sms);
+    if (rc != W4A8_OK) return rc;
+    QuantParams q{};
+    q.x = static_cast<const uint16_t*>(x);
+    q.ldx = ldx;
+    q.M = static_cast<int>(M);
+    q.K = static_cast<int>(K);
+    q.Kpad = static_cast<int>(kpad_of(K, gk));
+    q.G = static_cast<int>(cdiv(K, gk));
+    q.gk = gk;
+    q.rows = static_cast<int>(M);
+    q.vec_ok = aligned(x, 16) && (K % 8 == 0) && (ldx % 8 == 0);
+    q.q = a_q;
+    q.scale = a_scale;
+    q.scale_f32 = scale_dtype == W4A8_DTYPE_F32;
+    q.ksum = a_ksum;
+    const cudaError_t e = launch_quant_act(q, kOutPublic, static_cast<cudaStream_t>(stream), true);
+    return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
+}
+
+int w4a8_midgroup_quant_a(const void* x, int64_t M, int64_t K, int32_t gk, int64_t Mp, int8_t* a_hi, int8_t* a_lo,
+                          void* a_scale, int32_t* a_ksum, void* stream)
+{
+    if (M < 0 || K <= 0 || Mp < M) return W4A8_ERR_INVALID;
+    if (!group_ok(gk)) return W4A8_ERR_UNSUPPORTED;
+    if (Mp == 0) return W4A8_OK;
+    if (!x || !a_hi || !a_lo || !a_scale || !a_ksum || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if (!aligned(a_hi, 4) || !aligned(a_lo, 4) || !aligned(a_scale, 2) || !aligned(a_ksum, 4)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    int rc = device_info(&sms);
+    if (rc != W4A8_OK) return rc;
+    QuantParams q{};
+    q.x = static_cast<const uint16_t*>(x);
+    q.ldx = K;
+    q.M = static_cast<int>(M);
+    q.K = static_cast<int>(K);
+    q.Kpad = static_cast<int>(kpad_of(K, gk));
+    q.G = static_cast<int>(cdiv(K, gk));
+    q.gk = gk;
+    q.rows = static_cast<int>(Mp);
+    q.vec_ok = aligned(x, 16) && (K % 8 == 0);
+    q.a_hi = a_hi;
+    q.a_lo = a_lo;
+    q.a_scale = static_cast<uint16_t*>(a_scale);
+    q.a_ksum = a_ksum;
+    const cudaError_t e = launch_quant_act(q, kOutMsd, static_cast<cudaStream_t>(stream), true);
+    return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
+}
+
+int w4a8_midgroup_w4a8_gemm(const int8_t* a_hi, const int8_t* a_lo, const void* a_scale, const int32_t* a_ksum,
+                            int64_t M, const int8_t* w_q, const void* w_scale, const int32_t* w_ksum,
+                            const void* w_zero, int64_t N, int64_t K, int32_t gk, void* y, void* workspace,
+                            size_t workspace_bytes, void* stream)
+{
+    (void)a_ksum;
+    (void)w_ksum;
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!a_hi || !a_lo || !a_scale || !y || !aligned(a_hi, 4) || !aligned(a_lo, 4) || !aligned(a_scale, 2))
+        return W4A8_ERR_INVALID;
+    if ((rc = check_weights(w_q, w_scale, W4A8_DTYPE_BF16, w_zero)) != W4A8_OK) return rc;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    MsdToKernelParams m{};
+    m.a_hi = a_hi;
+    m.a_lo = a_lo;
+    m.a_scale = static_cast<const uint16_t*>(a_scale);
+    m.scale_ld = static_cast<int>(M);
+    m.M = static_cast<int>(M);
+    m.Kpad = static_cast<int>(pl.Kpad);
+    m.G = static_cast<int>(pl.G);
+    m.gk = gk;
+    m.aq = reinterpret_cast<int8_t*>(ws + pl.off_aq);
+    m.as = reinterpret_cast<float*>(ws + pl.off_as);
+    m.as_ld = pl.as_ld;
+    cudaError_t e = launch_msd_to_kernel(m, st, true);
+    if (e != cudaSuccess) return fail_cuda(e);
+    return run_gemm(pl, w_q, w_scale, W4A8_DTYPE_BF16, w_zero, y, N, false, ws, st);
+}
+
+int w4a8_workspace_status(void* workspace, int32_t reset, void* stream)
+{
+    if (!workspace) return W4A8_ERR_WORKSPACE;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail_cuda(e);
+    if (reset && v != 0) {
+        e = cudaMemsetAsync(workspace, 0, sizeof(int), st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return fail_cuda(e);
+    }
+    return v;
+}
+
+const char* w4a8_status_string(int s)
+{
+    switch (s) {
+        case W4A8_OK: return "ok";
+        case W4A8_ERR_INVALID: return "invalid argument (shape, null or misaligned pointer)";
+        case W4A8_ERR_UNSUPPORTED: return "unsupported group size or dtype";
+        case W4A8_ERR_CUDA: return "CUDA call failed (see w4a8_last_cuda_error)";
+        case W4A8_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+        case W4A8_ERR_DEVICE: return "current device is not an sm_100 GPU";
+        default: return s >= 0x100 ? "a kernel pipeline wait timed out" : "unknown status";
+    }
+}
+
+int w4a8_last_cuda_error(void) { return g_last_cuda; }
+
+int w4a8_build_arch(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,665 @@
+// w4a8_gemm.cu -- the mid-group W4A8 GEMM for sm_100a.
+//
+//   y[m, n] = sum_g  as[g, m] * ws[g, n] * P[g, m, n]
+//   P[g, m, n] = sum_{k in g} A_q[m, k] * (W_q[n, k] - wz[g, n])        (int32, exact)
+//
+// which is the reference's mid-group GEMM (fakequant_lab/fake_linear.py:155-179,
+// npu_ops/kernel/midgroup_w4a8_gemm.inc:1-60) computed without its MSD split:
+// B200's tensor core multiplies int8 x int8 natively (tcgen05 kind::i8).
+//
+// Mapping onto the tensor core (one CTA per SM, persistent):
+//   * MMA M = 128 weight rows (output channels), MMA N = TT tokens, K = 32/instr.
+//   * A operand = weights.  Packed int4 rows arrive by TMA into shared memory;
+//     four converter warps unpack them to int8 in registers and store them into
+//     tensor memory (tcgen05.st), so converted weights never make a second trip
+//     through shared memory.  Symmetric weights with GK <= 256 are unpacked as
+//     16*w (a nibble shifted into the top of its byte: 3 logic ops per 8
+//     weights); otherwise as the int8 value w - zero.
+//   * B operand = int8 activations from the quantiser (already in the order the
+//     unpack produces: k0 k2 k4 k6 k1 k3 k5 k7 per 8), TMA-loaded with 128-byte
+//     swizzle.
+//   * Each K-group accumulates into its own int32 TMEM buffer (two, so the MMA
+//     of group g+1 overlaps the rescale of group g).  For GK <= 256 the buffer
+//     is pre-set to the bits of 1.5*2^23, so float(P) is one exact fp32
+//     subtraction in the epilogue.
+//   * Epilogue warps: tcgen05.ld the int32 partials, acc += P * (ws * as) in
+//     fp32 registers, bf16 store at the end of the tile.
+//   * Work split: stream-K over (tile, K-unit) so every SM gets the same number
+//     of weight bytes.  A tile split across CTAs is reduced deterministically
+//     by the last CTA to arrive (fixed summation order), which also resets the
+//     tile's counter for the next call.
+//   * Every mbarrier wait is bounded (w4a8_common.cuh).
+#include "w4a8_common.cuh"
+#include "w4a8_kernels.h"
+
+namespace w4a8 {
+
+namespace {
+
+constexpr int kWStageBytes = 128 * 128;   // 128 weight rows x 128 B (256 int4)
+constexpr int kNumPreWarps = 6;           // producer, MMA, 4 converters
+constexpr int kAccCol0 = 128;             // TMEM: A buffers in [0,128), accumulators after
+constexpr int kSmemBudget = 227 * 1024 - 1024;
+
+// wait-site ids for the status word
+enum { kWProdEmpty = 1, kWProdSlot, kWConvFull, kWConvAEmpty, kWConvSlot, kWMmaFull, kWMmaAFull,
+       kWMmaAccEmpty, kWEpiSlot, kWEpiAccFull, kWDrain };
+
+template <int TT_, int GK_, bool ASYM_>
+struct Cfg {
+    static constexpr int TT = TT_;
+    static constexpr int GK = GK_;
+    static constexpr bool ASYM = ASYM_;
+    static constexpr int GPK = GK <= 256 ? 256 / GK : 1;     // groups per unit
+    static constexpr int KPU = GK <= 256 ? 1 : GK / 256;     // k-blocks per unit (max)
+    static constexpr bool SYM16 = !ASYM && GK <= 256;
+    static constexpr bool MAGIC = GK <= 256;                 // magic-initialised accumulators
+    static constexpr int E = TT <= 64 ? 1 : 2;               // epilogue warpgroups
+    static constexpr int NC = TT / E;                        // accumulator columns per thread
+    static constexpr int THREADS = (kNumPreWarps + 4 * E) * 32;
+    static constexpr int A_STAGE = TT * 256;
+    static constexpr int STAGE = kWStageBytes + A_STAGE;
+    __host__ __device__ static constexpr int r128(int x) { return (x + 127) / 128 * 128; }
+    static constexpr int SL_WS = GPK * 128 * 4;              // sized for fp32 scales
+    static constexpr int SL_WZ = ASYM ? GPK * 128 * 2 : 0;
+    static constexpr int SL_AS = GPK * TT * 4;
+    static constexpr int SLOT = r128(SL_WS) + r128(SL_WZ) + r128(SL_AS);
+    static constexpr int DS = 4;                             // scale slots
+    static constexpr int S_FIT = (kSmemBudget - DS * SLOT - 1024) / STAGE;
+    static constexpr int S = S_FIT > 8 ? 8 : S_FIT;          // pipeline stages
+    static constexpr int BAR_OFF = S * STAGE + DS * SLOT;
+    static constexpr int SMEM = BAR_OFF + 512 + 1024;        // + barriers + alignment slack
+    static constexpr int TMEM_COLS = (kAccCol0 + 2 * TT) <= 256 ? 256 : 512;
+    static_assert(S >= 3, "pipeline too shallow");
+};
+
+struct Bars {
+    uint64_t full[8], empty[8];
+    uint64_t sfull[4], sempty[4];
+    uint64_t afull[2], aempty[2];
+    uint64_t accfull[2], accempty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+    int last_flag;
+};
+
+static_assert(sizeof(Bars) <= 512, "barrier block overflows its reservation");
+
+struct Unit {
+    int t, wt, tt, ut;
+};
+
+// Bounded wait taken by a whole warp; the verdict is made warp-uniform so the
+// warp stays converged for the .sync.aligned tcgen05 instructions that follow.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int where)
+{
+    const bool ok = mbar_wait(bar, parity, abort_flag, status, where);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ Unit unit_of(const GemmParams& p, int u)
+{
+    Unit r;
+    r.t = u / p.units_per_tile;
+    r.ut = u - r.t * p.units_per_tile;
+    r.wt = r.t / p.n_tt;
+    r.tt = r.t - r.wt * p.n_tt;
+    return r;
+}
+
+template <class C>
+__device__ __forceinline__ void unit_kblocks(const GemmParams& p, int ut, int& kb0, int& kb1)
+{
+    if (C::GK <= 256) {
+        kb0 = ut;
+        kb1 = ut + 1;
+    } else {
+        kb0 = ut * C::KPU;
+        kb1 = min(kb0 + C::KPU, p.kb_total);
+    }
+}
+
+template <class C>
+__device__ __forceinline__ void unit_groups(const GemmParams& p, int ut, int& g0, int& g1)
+{
+    g0 = ut * C::GPK;
+    g1 = min(g0 + C::GPK, p.G);
+}
+
+__device__ __forceinline__ void cta_range(const GemmParams& p, int c, int C, int& u0, int& u1)
+{
+    u0 = static_cast<int>(static_cast<int64_t>(c) * p.total_units / C);
+    u1 = static_cast<int>(static_cast<int64_t>(c + 1) * p.total_units / C);
+}
+
+// The CTA whose range holds unit u (inverse of cta_range).
+__device__ __forceinline__ int cta_of_unit(const GemmParams& p, int u, int C)
+{
+    return static_cast<int>((static_cast<int64_t>(u + 1) * C - 1) / p.total_units);
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+template <int TT, int GK, bool ASYM>
+__global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
+    w4a8_gemm_kernel(const __grid_constant__ GemmParams p, const int ws_bf16, const int out_partials)
+{
+    using C = Cfg<TT, GK, ASYM>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars* bars = reinterpret_cast<Bars*>(smem + C::BAR_OFF);
+
+    const int warp = static_cast<int>(warp_id());
+    const int lane = static_cast<int>(lane_id());
+    const int nctas = static_cast<int>(gridDim.x);
+    const int cta = static_cast<int>(blockIdx.x);
+    int u0, u1;
+    cta_range(p, cta, nctas, u0, u1);
+
+    auto w_stage = [&](int s) { return smem + s * C::STAGE; };
+    auto a_stage = [&](int s) { return smem + s * C::STAGE + kWStageBytes; };
+    auto slot_ws = [&](int s) { return smem + C::S * C::STAGE + s * C::SLOT; };
+    auto slot_wz = [&](int s) { return slot_ws(s) + C::r128(C::SL_WS); };
+    auto slot_as = [&](int s) { return reinterpret_cast<float*>(slot_wz(s) + C::r128(C::SL_WZ)); };
+
+    // ---------------------------------------------------------------- setup
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < C::S; ++i) {
+            mbar_init(&bars->full[i], 1);
+            mbar_init(&bars->empty[i], 4 + 1);          // 4 converter warps + MMA commit
+        }
+        for (int i = 0; i < C::DS; ++i) {
+            mbar_init(&bars->sfull[i], 1);
+            mbar_init(&bars->sempty[i], 4 + 4 * C::E);  // converter + epilogue warps
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars->afull[i], 4);
+            mbar_init(&bars->aempty[i], 1);
+            mbar_init(&bars->accfull[i], 1);
+            mbar_init(&bars->accempty[i], 4 * C::E);
+        }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = bars->tmem_base;
+    volatile int* abort_flag = &bars->abort;
+    pdl_launch_dependents();
+
+    const uint32_t ws_elt = ws_bf16 ? 2u : 4u;
+    const uint32_t slot_tx = static_cast<uint32_t>(C::GPK * 128) * ws_elt +
+                             (C::ASYM ? C::GPK * 128 * 2 : 0) + C::GPK * C::TT * 4;
+
+    if (warp == 0) {
+        // ============================================================ producer
+        if (elect_one()) {
+            tma_prefetch_desc(&p.tm_w);
+            tma_prefetch_desc(&p.tm_a);
+            tma_prefetch_desc(&p.tm_ws);
+            tma_prefetch_desc(&p.tm_as);
+            if (C::ASYM) tma_prefetch_desc(&p.tm_wz);
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_a = policy_evict_last();
+            int last_par[8], slot_par[4];
+            for (int i = 0; i < 8; ++i) last_par[i] = -1;
+            for (int i = 0; i < 4; ++i) slot_par[i] = -1;
+            bool ok = true;
+
+            // Walk state: (u, kbi) -> stage / slot indices.
+            int u = u0, kbi = 0, stage = 0, slot = 0;
+            uint32_t sph = 0, slph = 0;
+            // --- phase 1: weight-side loads, before the producer of x has finished (PDL) ---
+            int pre = 0, pre_units = 0;
+            {
+                int uu = u0, kk = 0;
+                while (uu < u1 && pre < C::S) {
+                    const Unit un = unit_of(p, uu);
+                    int kb0, kb1;
+                    unit_kblocks<C>(p, un.ut, kb0, kb1);
+                    if (kk == 0) {
+                        if (pre_units >= C::DS) break;
+                        const int sl = pre_units;
+                        mbar_arrive_expect_tx(&bars->sfull[sl], slot_tx);
+                        tma_load_2d(slot_ws(sl), &p.tm_ws, &bars->sfull[sl], un.wt * 128, un.ut * C::GPK);
+                        if (C::ASYM)
+                            tma_load_2d(slot_wz(sl), &p.tm_wz, &bars->sfull[sl], un.wt * 128, un.ut * C::GPK);
+                        slot_par[sl] = 0;
+                        ++pre_units;
+                    }
+                    const int kbg = kb0 + kk;
+                    mbar_arrive_expect_tx(&bars->full[pre], C::STAGE);
+                    tma_load_2d_hint(w_stage(pre), &p.tm_w, &bars->full[pre], kbg * 128, un.wt * 128, pol_w);
+                    last_par[pre] = 0;
+                    ++pre;
+                    if (++kk >= kb1 - kb0) { ++uu; kk = 0; }
+                }
+            }
+            pdl_wait();
+            // --- phase 2: the activation-side loads of the pre-issued stages ---
+            {
+                int uu = u0, kk = 0, n = 0, nu = 0;
+                while (n < pre) {
+                    const Unit un = unit_of(p, uu);
+                    int kb0, kb1;
+                    unit_kblocks<C>(p, un.ut, kb0, kb1);
+                    if (kk == 0) {
+                        tma_load_2d_hint(slot_as(nu), &p.tm_as, &bars->sfull[nu], un.tt * C::TT,
+                                         un.ut * C::GPK, pol_a);
+                        ++nu;
+                    }
+                    const int kbg = kb0 + kk;
+                    tma_load_2d_hint(a_stage(n), &p.tm_a, &bars->full[n], kbg * 256, un.tt * C::TT, pol_a);
+                    tma_load_2d_hint(a_stage(n) + C::TT * 128, &p.tm_a, &bars->full[n], kbg * 256 + 128,
+                                     un.tt * C::TT, pol_a);
+                    ++n;
+                    if (++kk >= kb1 - kb0) { ++uu; kk = 0; }
+                }
+                u = uu;
+                kbi = kk;
+                stage = pre % C::S;
+                sph = (pre / C::S) & 1;
+                slot = pre_units % C::DS;
+                slph = (pre_units / C::DS) & 1;
+            }
+            // --- steady state ---
+            while (ok && u < u1) {
+                const Unit un = unit_of(p, u);
+                int kb0, kb1;
+                unit_kblocks<C>(p, un.ut, kb0, kb1);
+                if (kbi == 0) {
+                    if (!mbar_wait(&bars->sempty[slot], slph ^ 1, abort_flag, p.status, kWProdSlot)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&bars->sfull[slot], slot_tx);
+                    tma_load_2d(slot_ws(slot), &p.tm_ws, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
+                    if (C::ASYM)
+                        tma_load_2d(slot_wz(slot), &p.tm_wz, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
+                    tma_load_2d_hint(slot_as(slot), &p.tm_as, &bars->sfull[slot], un.tt * C::TT,
+                                     un.ut * C::GPK, pol_a);
+                    slot_par[slot] = static_cast<int>(slph);
+                    if (++slot == C::DS) { slot = 0; slph ^= 1; }
+                }
+                if (!mbar_wait(&bars->empty[stage], sph ^ 1, abort_flag, p.status, kWProdEmpty)) { ok = false; break; }
+                const int kbg = kb0 + kbi;
+                mbar_arrive_expect_tx(&bars->full[stage], C::STAGE);
+                tma_load_2d_hint(w_stage(stage), &p.tm_w, &bars->full[stage], kbg * 128, un.wt * 128, pol_w);
+                tma_load_2d_hint(a_stage(stage), &p.tm_a, &bars->full[stage], kbg * 256, un.tt * C::TT, pol_a);
+                tma_load_2d_hint(a_stage(stage) + C::TT * 128, &p.tm_a, &bars->full[stage], kbg * 256 + 128,
+                                 un.tt * C::TT, pol_a);
+                last_par[stage] = static_cast<int>(sph);
+                if (++stage == C::S) { stage = 0; sph ^= 1; }
+                if (++kbi >= kb1 - kb0) { ++u; kbi = 0; }
+            }
+            // Never leave with a copy in flight: wait (bounded) for the last load of every buffer.
+            for (int i = 0; i < C::S; ++i)
+                if (last_par[i] >= 0) mbar_wait(&bars->full[i], static_cast<uint32_t>(last_par[i]), abort_flag, p.status, kWDrain);
+            for (int i = 0; i < C::DS; ++i)
+                if (slot_par[i] >= 0) mbar_wait(&bars->sfull[i], static_cast<uint32_t>(slot_par[i]), abort_flag, p.status, kWDrain);
+        }
+    } else if (warp == 1) {
+        // ============================================================ MMA issuer
+        if (elect_one()) {
+            const uint32_t idesc = idesc_i8(128, TT);
+            int stage = 0, ab = 0, accb = 0;
+            uint32_t sph = 0, abph = 0, accph = 0;
+            bool ok = true;
+            for (int u = u0; ok && u < u1; ++u) {
+                const Unit un = unit_of(p, u);
+                int kb0, kb1, g0, g1;
+                unit_kblocks<C>(p, un.ut, kb0, kb1);
+                unit_groups<C>(p, un.ut, g0, g1);
+                for (int kbg = kb0; kbg < kb1; ++kbg) {
+                    if (!mbar_wait(&bars->full[stage], sph, abort_flag, p.status, kWMmaFull)) { ok = false; break; }
+                    if (!mbar_wait(&bars->afull[ab], abph, abort_flag, p.status, kWMmaAFull)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_smem = smem_u32(a_stage(stage));
+                    const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * 64);
+                    if (C::GK <= 256) {
+                        for (int g = g0; g < g1; ++g) {
+                            if (!mbar_wait(&bars->accempty[accb], accph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                            tc_fence_after();
+                            const uint32_t d_tmem = tbase + kAccCol0 + static_cast<uint32_t>(accb * TT);
+                            const int ks0 = (g - g0) * (C::GK / 32);
+#pragma unroll
+                            for (int j = 0; j < C::GK / 32; ++j) {
+                                const int ks = ks0 + j;
+                                const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
+                                tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, 1u);
+                            }
+                            tc_commit(&bars->accfull[accb]);
+                            if (++accb == 2) { accb = 0; accph ^= 1; }
+                        }
+                        if (!ok) break;
+                    } else {
+                        const bool first = (kbg == kb0), last = (kbg == kb1 - 1);
+                        if (first) {
+                            if (!mbar_wait(&bars->accempty[accb], accph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                            tc_fence_after();
+                        }
+                        const uint32_t d_tmem = tbase + kAccCol0 + static_cast<uint32_t>(accb * TT);
+#pragma unroll
+                        for (int ks = 0; ks < 8; ++ks) {
+                            const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
+                            tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, (first && ks == 0) ? 0u : 1u);
+                        }
+                        if (last) {
+                            tc_commit(&bars->accfull[accb]);
+                            if (++accb == 2) { accb = 0; accph ^= 1; }
+                        }
+                    }
+                    tc_commit(&bars->aempty[ab]);
+                    tc_commit(&bars->empty[stage]);
+                    if (++ab == 2) { ab = 0; abph ^= 1; }
+                    if (++stage == C::S) { stage = 0; sph ^= 1; }
+                }
+            }
+            // Wait for every MMA issued by this thread before TMEM can be released.
+            tc_commit(&bars->drain);
+            mbar_wait(&bars->drain, 0, abort_flag, p.status, kWDrain);
+        }
+    } else if (warp < kNumPreWarps) {
+        // ============================================================ converters
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        int stage = 0, ab = 0, slot = 0;
+        uint32_t sph = 0, abph = 0, slph = 0;
+        bool ok = true;
+        for (int u = u0; ok && u < u1; ++u) {
+            const Unit un = unit_of(p, u);
+            int kb0, kb1;
+            unit_kblocks<C>(p, un.ut, kb0, kb1);
+            uint32_t bias[C::GPK];
+#pragma unroll
+            for (int i = 0; i < C::GPK; ++i) bias[i] = 0x78787878u;   // zero point 0
+            if (C::ASYM) {
+                if (!warp_wait(&bars->sfull[slot], slph, abort_flag, p.status, kWConvSlot)) { ok = false; break; }
+                const uint16_t* wz = reinterpret_cast<const uint16_t*>(slot_wz(slot));
+#pragma unroll
+                for (int i = 0; i < C::GPK; ++i) {
+                    const int zu = static_cast<int>(bf16_bits_to_f32(wz[i * 128 + row])) + 8;
+                    bias[i] = static_cast<uint32_t>((0x80 - zu) & 0xFF) * 0x01010101u;
+                }
+            }
+            for (int kbg = kb0; kbg < kb1; ++kbg) {
+                if (!warp_wait(&bars->full[stage], sph, abort_flag, p.status, kWConvFull)) { ok = false; break; }
+                if (!warp_wait(&bars->aempty[ab], abph ^ 1, abort_flag, p.status, kWConvAEmpty)) { ok = false; break; }
+                tc_fence_after();
+                const uint8_t* wrow = w_stage(stage) + row * 128;
+                const uint32_t a_tmem = tbase + lane_off + static_cast<uint32_t>(ab * 64);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                    uint32_t o[8];
+                    // chunk c holds K positions [32c, 32c+32) of this k-block
+                    const uint32_t bz = bias[C::GK <= 256 ? (c * 32) / (C::GK <= 256 ? C::GK : 256) : 0];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (C::SYM16) {
+                            o[2 * j] = (w[j] << 4) & 0xF0F0F0F0u;       // 16 * even-k weights
+                            o[2 * j + 1] = w[j] & 0xF0F0F0F0u;          // 16 * odd-k weights
+                        } else {
+                            const uint32_t x = w[j] ^ 0x88888888u;     // nibble + 8 in [0, 15]
+                            o[2 * j] = ((x & 0x0F0F0F0Fu) + bz) ^ 0x80808080u;
+                            o[2 * j + 1] = (((x >> 4) & 0x0F0F0F0Fu) + bz) ^ 0x80808080u;
+                        }
+                    }
+                    tc_st8(a_tmem + c * 8, o);
+                }
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&bars->afull[ab]);
+                    mbar_arrive(&bars->empty[stage]);
+                }
+                __syncwarp();
+                if (++ab == 2) { ab = 0; abph ^= 1; }
+                if (++stage == C::S) { stage = 0; sph ^= 1; }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->sempty[slot]);
+            if (++slot == C::DS) { slot = 0; slph ^= 1; }
+        }
+    } else {
+        // ============================================================ epilogue
+        const int ew = warp - kNumPreWarps;
+        const int quarter = warp & 3;
+        const int half = ew >> 2;
+        const int row = quarter * 32 + lane;
+        const int col0 = half * C::NC;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        constexpr int NCH = C::NC / 16;
+        const int nthr = 4 * C::E * 32;
+
+        if (C::MAGIC) {
+#pragma unroll
+            for (int b = 0; b < 2; ++b)
+#pragma unroll
+                for (int i = 0; i < NCH; ++i)
+                    tc_st16_fill(tbase + lane_off + kAccCol0 + b * TT + col0 + 16 * i, kMagicBits);
+            tc_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&bars->accempty[0]);
+            mbar_arrive(&bars->accempty[1]);
+        }
+
+        float acc[C::NC];
+#pragma unroll
+        for (int j = 0; j < C::NC; ++j) acc[j] = 0.0f;
+        int slot = 0, accb = 0;
+        uint32_t slph = 0, accph = 0;
+        bool ok = true;
+        for (int u = u0; ok && u < u1; ++u) {
+            const Unit un = unit_of(p, u);
+            int g0, g1;
+            unit_groups<C>(p, un.ut, g0, g1);
+            if (!warp_wait(&bars->sfull[slot], slph, abort_flag, p.status, kWEpiSlot)) { ok = false; break; }
+            const uint8_t* wsb = slot_ws(slot);
+            const float* asb = slot_as(slot);
+            for (int g = g0; g < g1; ++g) {
+                const int gi = g - g0;
+                float wsv = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gi * 128 + row])
+                                    : reinterpret_cast<const float*>(wsb)[gi * 128 + row];
+                if (C::SYM16) wsv *= 0.0625f;   // the unpack carried weights as 16*w
+                if (!warp_wait(&bars->accfull[accb], accph, abort_flag, p.status, kWEpiAccFull)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t t_acc = tbase + lane_off + kAccCol0 + static_cast<uint32_t>(accb * TT + col0);
+                const float* asg = asb + gi * TT + col0;
+#pragma unroll
+                for (int i = 0; i < NCH; ++i) {
+                    uint32_t r[16];
+                    tc_ld16(t_acc + 16 * i, r);
+                    tc_wait_ld();
+                    if (C::MAGIC) tc_st16_fill(t_acc + 16 * i, kMagicBits);
+                    if (!out_partials) {
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 a4 = *reinterpret_cast<const float4*>(asg + 16 * i + 4 * j4);
+                            const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj) {
+                                const int j = 4 * j4 + jj;
+                                const float f = C::MAGIC ? (__uint_as_float(r[j]) - kMagicF)
+                                                         : static_cast<float>(static_cast<int>(r[j]));
+                                acc[16 * i + j] = fmaf(f, wsv * av[jj], acc[16 * i + j]);
+                            }
+                        }
+                    } else {
+                        const int n = un.wt * 128 + row;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int m = un.tt * TT + col0 + 16 * i + j;
+                            int P = C::MAGIC ? static_cast<int>(r[j] - kMagicBits) : static_cast<int>(r[j]);
+                            if (C::SYM16) P >>= 4;
+                            if (m < p.M && n < p.N)
+                                reinterpret_cast<int*>(p.out)[(static_cast<int64_t>(g) * p.M + m) * p.N + n] = P;
+                        }
+                    }
+                }
+                if (C::MAGIC) tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->accempty[accb]);
+                __syncwarp();
+                if (++accb == 2) { accb = 0; accph ^= 1; }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->sempty[slot]);
+            if (++slot == C::DS) { slot = 0; slph ^= 1; }
+
+            // ---- end of this CTA's share of tile t: store or hand over ----
+            if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
+                if (!out_partials) {
+                    const int t = un.t;
+                    const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
+                    const int n = un.wt * 128 + row;
+                    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
+                    if (u0 <= tfirst && u1 - 1 >= tlast) {
+#pragma unroll
+                        for (int j = 0; j < C::NC; ++j) {
+                            const int m = un.tt * TT + col0 + j;
+                            if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(acc[j]);
+                        }
+                    } else {
+                        const int side = (t == u0 / p.units_per_tile) ? 0 : 1;
+                        float* mine = p.partials + static_cast<int64_t>(2 * cta + side) * (TT * 128);
+#pragma unroll
+                        for (int j = 0; j < C::NC; ++j) mine[(col0 + j) * 128 + row] = acc[j];
+                        __threadfence();
+                        named_bar_sync(1, nthr);
+                        const int cf = cta_of_unit(p, tfirst, nctas), cl = cta_of_unit(p, tlast, nctas);
+                        if (ew == 0 && lane == 0) {
+                            const int old = atomicAdd(&p.counters[t], 1);
+                            bars->last_flag = (old == cl - cf) ? 1 : 0;
+                        }
+                        named_bar_sync(1, nthr);
+                        if (bars->last_flag) {
+                            __threadfence();
+                            float sum[C::NC];
+#pragma unroll
+                            for (int j = 0; j < C::NC; ++j) sum[j] = 0.0f;
+                            for (int c2 = cf; c2 <= cl; ++c2) {
+                                int cu0, cu1;
+                                cta_range(p, c2, nctas, cu0, cu1);
+                                const int s2 = (t == cu0 / p.units_per_tile) ? 0 : 1;
+                                const float* src = p.partials + static_cast<int64_t>(2 * c2 + s2) * (TT * 128);
+#pragma unroll
+                                for (int j = 0; j < C::NC; ++j) sum[j] += __ldcg(src + (col0 + j) * 128 + row);
+                            }
+#pragma unroll
+                            for (int j = 0; j < C::NC; ++j) {
+                                const int m = un.tt * TT + col0 + j;
+                                if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
+                            }
+                            if (ew == 0 && lane == 0) p.counters[t] = 0;
+                        }
+                        named_bar_sync(1, nthr);   // last_flag is reused by the next tile
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < C::NC; ++j) acc[j] = 0.0f;
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, C::TMEM_COLS);
+    }
+}
+
+template <int TT, int GK, bool ASYM>
+cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pdl, int ws_bf16,
+                     int out_partials)
+{
+    using C = Cfg<TT, GK, ASYM>;
+    auto kern = w4a8_gemm_kernel<TT, GK, ASYM>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, p, ws_bf16, out_partials);
+}
+
+template <int TT, int GK>
+cudaError_t launch_gk(const GemmParams& p, const GemmConfig& c, int grid, cudaStream_t s, bool pdl)
+{
+    return c.asym ? launch_t<TT, GK, true>(p, grid, s, pdl, c.ws_bf16, c.partials)
+                  : launch_t<TT, GK, false>(p, grid, s, pdl, c.ws_bf16, c.partials);
+}
+
+template <int TT>
+cudaError_t launch_tt(const GemmParams& p, const GemmConfig& c, int grid, cudaStream_t s, bool pdl)
+{
+    switch (c.gk) {
+        case 64: return launch_gk<TT, 64>(p, c, grid, s, pdl);
+        case 128: return launch_gk<TT, 128>(p, c, grid, s, pdl);
+        case 256: return launch_gk<TT, 256>(p, c, grid, s, pdl);
+        case 1024: return launch_gk<TT, 1024>(p, c, grid, s, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int TT>
+size_t smem_tt(int gk, bool asym)
+{
+    switch (gk) {
+        case 64: return asym ? Cfg<TT, 64, true>::SMEM : Cfg<TT, 64, false>::SMEM;
+        case 128: return asym ? Cfg<TT, 128, true>::SMEM : Cfg<TT, 128, false>::SMEM;
+        case 256: return asym ? Cfg<TT, 256, true>::SMEM : Cfg<TT, 256, false>::SMEM;
+        default: return asym ? Cfg<TT, 1024, true>::SMEM : Cfg<TT, 1024, false>::SMEM;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_gemm(const GemmParams& p, const GemmConfig& c, int grid, cudaStream_t stream, bool pdl)
+{
+    switch (c.tt) {
+        case 16: return launch_tt<16>(p, c, grid, stream, pdl);
+        case 32: return launch_tt<32>(p, c, grid, stream, pdl);
+        case 64: return launch_tt<64>(p, c, grid, stream, pdl);
+        case 128: return launch_tt<128>(p, c, grid, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+size_t gemm_smem_bytes(const GemmConfig& c)
+{
+    switch (c.tt) {
+        case 16: return smem_tt<16>(c.gk, c.asym);
+        case 32: return smem_tt<32>(c.gk, c.asym);
+        case 64: return smem_tt<64>(c.gk, c.asym);
+        default: return smem_tt<128>(c.gk, c.asym);
+    }
+}
+
+}  // namespace w4a8
