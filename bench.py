@@ -1,0 +1,418 @@
+"""Benchmark of the B200 W4A8 mid-group linear layer.
+
+Headline (N=1): the decode sweep of BASELINE config 1 -- the four QwQ-32B
+projections (qkv, o, gate_up, down) at M in {1,4,8,16,32,64}, int4 group-128
+symmetric weights with fp32 per-group scales, bf16 activations quantised per
+(token, group) inside the op.  One step = those 24 linear calls (quantiser +
+GEMM each), shapes interleaved so every weight matrix is evicted from L2
+before its next use (244 MB of weights per step > 126 MB L2).  The metric is
+algorithmic HBM GB/s: sum over calls of N*K/2 + G*N*4 + M*K*2 + M*N*2 bytes,
+divided by the step time.
+
+  value          device time of K CUDA-graph replays of the step (inputs resident)
+  e2e            the same step through the public op with host buffers: per call
+                 a pinned host->device copy of x and a device->host copy of y
+  roofline       the GEMM kernel alone, each launch timed with CUDA events after an
+                 L2 flush; achieved = algorithmic bytes / kernel time
+  prefill        BASELINE config 2 subset (M = 2048, 4096): GEMM int8 TOP/s against
+                 cuBLAS int8 (torch._int_mm) measured in the same run
+  cpu_baseline   the reference's own C++ CPU GEMM (oracle/_ref, compiled from the
+                 reference sources) plus the C port of its activation quantiser,
+                 on a 1/8-of-N sample of the same sweep, all host threads
+  tp_stack       (N > 1) BASELINE config 4: 4 QwQ-32B decoder-layer linear stacks,
+                 tensor-parallel over the N GPUs with NCCL all-reduce
+
+Multi-GPU: one process per GPU (torchrun).  Every rank runs its own replica of
+the sweep (weak scaling; the sweep has no exchange step) and the step time is
+the max over ranks; the tensor-parallel layer stack is reported beside it.
+
+``--impl reference`` times the reference's CPU implementation instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (REPO, os.path.join(REPO, "vllm-ascend910_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+GK = 128
+SHAPES = ["qkv", "o", "gate_up", "down"]
+DECODE_MS = (1, 4, 8, 16, 32, 64)
+PREFILL_MS = (2048, 4096)
+METRIC = "W4A8 GEMM HBM GB/s (decode)"
+
+
+def alg_bytes(M, N, K, gk=GK, scale_bytes=4, asym=False):
+    G = -(-K // gk)
+    return N * K // 2 + G * N * scale_bytes + (G * N * 2 if asym else 0) + M * K * 2 + M * N * 2
+
+
+def sweep_configs(ms=DECODE_MS):
+    return [(shape, M) for M in ms for shape in SHAPES]
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+
+def cpu_sample(n_div=8, ms=DECODE_MS, seed=0):
+    """The reference C++ GEMM (+ the C port of its quantiser) on a 1/n_div-of-N
+    sample of the sweep.  Returns (GB/s, seconds, threads, kind, description)."""
+    import oracle
+    from w4a8_b200 import synthetic as syn
+    from w4a8_b200.synthetic import QWQ_SHAPES
+    use_ref = oracle.ref_available()
+    data = []
+    for shape, M in sweep_configs(ms):
+        K, N = QWQ_SHAPES[shape]
+        Ns = N // n_div
+        xb = syn.activation_np(M, K, seed + M)
+        w = syn.weight_np(Ns, K, GK, seed + 7 + K)
+        data.append((M, Ns, K, xb, w, oracle.f32_to_bf16(w.scale)))
+    t0 = time.perf_counter()
+    tot = 0
+    for M, Ns, K, xb, w, wsb in data:
+        q, s, _ = oracle.quant_act(xb, GK)
+        if use_ref:
+            oracle.ref_midgroup_gemm(q, s, w.codes, wsb, None, GK)
+        else:
+            oracle.gemm_kernel_order(q, oracle.bf16_to_f32(s), w.codes, w.scale, None, GK)
+        tot += alg_bytes(M, Ns, K)
+    dt = time.perf_counter() - t0
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    kind = "reference" if use_ref else "port"
+    desc = (f"decode sweep (24 calls) with N/{n_div} weight rows per call; "
+            + ("ReferenceMidGroupGemm (int4_cube_lab/host/gemm_ref.cpp, -O3 -fopenmp) after the C port of "
+               "fakequant_lab's activation quantiser" if use_ref else "C port of the reference CPU path"))
+    return tot / dt / 1e9, dt, threads, kind, desc
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample()
+    for _ in range(args.steps):
+        v, dt, threads, kind, desc = cpu_sample()
+        vals.append((v, dt))
+    v = statistics.median(x[0] for x in vals)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * statistics.median(x[1] for x in vals), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+            "config": {"workload": "decode sweep, QwQ-32B qkv/o/gate_up/down x M in {1,4,8,16,32,64}, "
+                                   "GK=128 sym int4, per-step sample of N/8 weight rows"},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": kind, "sample": desc},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def build_weights(torch, dev, seed=0):
+    from w4a8_b200 import ops
+    from w4a8_b200.synthetic import QWQ_SHAPES, weight_torch
+    W = {}
+    for i, shape in enumerate(SHAPES):
+        K, N = QWQ_SHAPES[shape]
+        codes, scale, _ = weight_torch(N, K, GK, seed + i, dev)
+        W[shape] = (ops.pack_int4_grouped(codes, GK), scale.contiguous(), K, N)
+        del codes
+    return W
+
+
+def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=3):
+    """GEMM-only launches, L2 flushed before each, CUDA events on the launch stream."""
+    out = []
+    st = torch.cuda.current_stream()
+    for (shape, M) in cfgs:
+        packed, scale, K, N = W[shape]
+        x = xs[(shape, M)]
+        ts = []
+        for _ in range(reps):
+            ops.linear_quant(x, N, GK)
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            ops.linear_gemm(M, K, packed, scale, None, GK, ys[(shape, M)])
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e-3)
+        out.append((shape, M, K, N, min(ts)))
+    return out
+
+
+def int8_peak_tops(torch, dev):
+    a = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    b = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=dev).t()
+    try:
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = 1e9
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e-3)
+        return 2 * 8192 ** 3 / best / 1e12
+    except Exception:
+        return None
+
+
+def run_gpu(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hbm_peak, peak_src = peaks()
+    sampler = ClockSampler(local_rank)
+    W = build_weights(torch, dev, seed=rank)
+    cfgs = sweep_configs()
+    xs = {(s, M): syn.activation_torch(M, W[s][2], 100 + M, dev) for (s, M) in cfgs}
+    ys = {(s, M): torch.empty(M, W[s][3], dtype=torch.bfloat16, device=dev) for (s, M) in cfgs}
+    step_bytes = sum(alg_bytes(M, W[s][3], W[s][2]) for (s, M) in cfgs)
+
+    def step():
+        for (s, M) in cfgs:
+            packed, scale, K, N = W[s]
+            ops.linear(xs[(s, M)], packed, scale, None, GK, out=ys[(s, M)])
+
+    sampler.start()
+    step()                                     # allocates the workspace
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_step = e0.elapsed_time(e1) * 1e-3 / args.steps
+    if world > 1:
+        t = torch.tensor([t_step], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_step = float(t.item())
+    value = world * step_bytes / t_step / 1e9
+    status = ops.workspace_status(dev)
+
+    # ---- end to end through the public op, host buffers ----
+    xh = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    yh = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in ys.items()}
+    xd = {k: torch.empty_like(v) for k, v in xs.items()}
+    h2d = sum(v.numel() * 2 for v in xh.values())
+    d2h = sum(v.numel() * 2 for v in yh.values())
+
+    def e2e_step():
+        for (s, M) in cfgs:
+            packed, scale, K, N = W[s]
+            xd[(s, M)].copy_(xh[(s, M)], non_blocking=True)
+            y = ops.linear(xd[(s, M)], packed, scale, None, GK)
+            yh[(s, M)].copy_(y, non_blocking=True)
+
+    n_e2e = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(n_e2e):
+        e2e_step()
+    a1.record()
+    torch.cuda.synchronize()
+    t_e2e = a0.elapsed_time(a1) * 1e-3 / n_e2e
+    if world > 1:
+        t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_e2e = float(t.item())
+    e2e = {"value": world * step_bytes / t_e2e / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * t_e2e, "steps": n_e2e}
+
+    # ---- dominant kernel alone (GEMM), cold L2, events per launch ----
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    kt = time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush)
+    k_bytes = sum(alg_bytes(M, N, K) for (_, M, K, N, _) in kt)
+    k_time = sum(t for *_, t in kt)
+    achieved = k_bytes / k_time / 1e9
+    per_shape = [{"shape": s, "M": M, "us": round(t * 1e6, 2),
+                  "GBps": round(alg_bytes(M, N, K) / t / 1e9, 1),
+                  "frac": round(alg_bytes(M, N, K) / t / 1e9 / hbm_peak, 3)} for (s, M, K, N, t) in kt]
+    traffic = None
+    tfile = os.path.join(REPO, "profiles", "gemm_decode_traffic.json")
+    if os.path.exists(tfile):
+        tj = json.load(open(tfile))
+        traffic = tj.get("bytes_per_launch")
+
+    # ---- prefill subset: GEMM int8 TOP/s ----
+    pre = []
+    big = {}
+    for M in PREFILL_MS:
+        for s in SHAPES:
+            packed, scale, K, N = W[s]
+            x = syn.activation_torch(M, K, 200 + M, dev)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            big[(s, M)] = (x, y)
+    pk = time_kernels_cold(torch, ops, W, list(big.keys()), {k: v[0] for k, v in big.items()},
+                           {k: v[1] for k, v in big.items()}, flush, reps=2)
+    for (s, M, K, N, t) in pk:
+        pre.append({"shape": s, "M": M, "us": round(t * 1e6, 1), "TOPS": round(2 * M * N * K / t / 1e12, 1)})
+    del big
+    i8_peak = int8_peak_tops(torch, dev)
+    pre_tops = sum(2 * M * N * K for (_, M, K, N, _) in pk) / sum(t for *_, t in pk) / 1e12
+    clocks = sampler.stop()
+
+    # ---- tensor-parallel layer stack (config 4) ----
+    tp = None
+    if world > 1 or args.tp_stack:
+        from w4a8_b200 import tp as tpmod
+        tp = tpmod.bench_stack(world, rank, dev, ms=(16, 256, 4096), layers=4, iters=max(3, min(args.steps, 20)))
+
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v, dt, threads, kind, desc = cpu_sample()
+        cpu = {"value": v, "unit": "GB/s", "cores": threads, "kind": kind, "sample": desc,
+               "seconds": round(dt, 2)}
+    launches = 2 * len(cfgs) * args.steps
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * t_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+        "config": {"workload": "decode sweep (BASELINE config 1): QwQ-32B qkv/o/gate_up/down x M in "
+                               "{1,4,8,16,32,64}, int4 sym GK=128, fp32 lognormal scales, bf16 N(0,1) "
+                               "activations with 0.5% x20 outlier channels, quantised per (token, group) in-op",
+                   "calls_per_step": len(cfgs), "alg_bytes_per_step": step_bytes,
+                   "l2": "inputs larger than L2: 244 MB of weights per step, shapes interleaved",
+                   "timing": "CUDA graph of the step, events on the replay stream, max over ranks",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "kernel": "w4a8_gemm_kernel (GEMM alone, L2 flushed before each launch)",
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src},
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "prefill": {"metric": "W4A8 GEMM int8 TOP/s (prefill)", "value": pre_tops, "unit": "TOP/s",
+                    "int8_peak_measured_cublas": i8_peak,
+                    "frac_of_measured_int8": (pre_tops / i8_peak) if i8_peak else None,
+                    "frac_of_nominal_4500": pre_tops / 4500.0, "per_shape": pre},
+        "per_shape": per_shape,
+        "cpu_baseline": cpu,
+        "status_word": status,
+    }
+    if tp is not None:
+        line["tp_stack"] = tp
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--tp-stack", action="store_true", help="also run the TP layer stack at N=1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -6,8 +6,8 @@ raise ``RuntimeError`` with a message.  Kernels run on the current CUDA stream;
 nothing here synchronises, so every op is CUDA-graph capturable once its
 workspace exists.
 
-Workspaces: each (device, stream) keeps one zero-initialised scratch buffer,
-grown on demand outside graph capture (the kernels leave it reusable).
+Workspaces: each device keeps one zero-initialised scratch buffer, grown on
+demand outside graph capture (the kernels leave it reusable).
 """
 from __future__ import annotations
 
@@ -18,7 +18,7 @@ import torch
 from . import _lib
 
 GROUP = 1024          # the reference op's compile-time group size (w4a8_ops.py:60)
-_WS: Dict[Tuple[int, int], torch.Tensor] = {}
+_WS: Dict[int, torch.Tensor] = {}
 
 
 def num_groups(K: int, group_size: int = GROUP) -> int:
@@ -57,8 +57,13 @@ def _stream(device: torch.device) -> int:
 
 
 def workspace(nbytes: int, device: torch.device) -> Tuple[int, int]:
-    """(aligned pointer, usable bytes) of this stream's scratch buffer."""
-    key = (device.index if device.index is not None else torch.cuda.current_device(), _stream(device))
+    """(aligned pointer, usable bytes) of this device's scratch buffer.
+
+    One buffer per device: ops on one device are expected to run in stream
+    order (CUDA-graph capture included).  Callers that run W4A8 ops
+    concurrently on several streams of one device must give each stream its
+    own buffer through the C ABI."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
     buf = _WS.get(key)
     need = nbytes + 1024
     if buf is None or buf.numel() < need:
