@@ -382,6 +382,27 @@ def run_gpu(args, rank, world, local_rank):
     print(json.dumps(line))
 
 
+def profile_case(spec: str):
+    """One shape, a few launches: the target of the ncu captures (profiles/)."""
+    import torch
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    from w4a8_b200.synthetic import QWQ_SHAPES
+    shape, M = spec.split(":")
+    M = int(M)
+    K, N = QWQ_SHAPES[shape]
+    dev = torch.device("cuda", 0)
+    codes, scale, _ = syn.weight_torch(N, K, GK, 1, dev)
+    packed = ops.pack_int4_grouped(codes, GK)
+    x = syn.activation_torch(M, K, 2, dev)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    for _ in range(8):
+        ops.linear(x, packed, scale, None, GK, out=y)
+    torch.cuda.synchronize()
+    assert ops.workspace_status(dev) == 0
+    print(f"profile case {shape} M={M} K={K} N={N}: ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -390,7 +411,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tp-stack", action="store_true", help="also run the TP layer stack at N=1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", default=None, help="SHAPE:M, e.g. qkv:16 (ncu target)")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
