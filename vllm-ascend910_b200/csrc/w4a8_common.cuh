@@ -266,6 +266,46 @@ __host__ __device__ constexpr uint32_t idesc_i8(uint32_t M, uint32_t N)
            | ((M >> 4) << 24);   // M / 16
 }
 
+// ---------------------------------------------------------------- packed fp32 pairs
+// sm_100 executes two fp32 lanes per instruction on a 64-bit register pair.
+
+__device__ __forceinline__ uint64_t pack2(float lo, float hi)
+{
+    return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+
+__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi)
+{
+    return static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
+}
+
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi)
+{
+    lo = __uint_as_float(static_cast<uint32_t>(v));
+    hi = __uint_as_float(static_cast<uint32_t>(v >> 32));
+}
+
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 // ---------------------------------------------------------------- misc
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b)

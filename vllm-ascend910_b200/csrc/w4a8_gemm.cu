@@ -18,12 +18,14 @@
 //   * B operand = int8 activations from the quantiser (already in the order the
 //     unpack produces: k0 k2 k4 k6 k1 k3 k5 k7 per 8), TMA-loaded with 128-byte
 //     swizzle.
-//   * Each K-group accumulates into its own int32 TMEM buffer (two, so the MMA
-//     of group g+1 overlaps the rescale of group g).  For GK <= 256 the buffer
-//     is pre-set to the bits of 1.5*2^23, so float(P) is one exact fp32
-//     subtraction in the epilogue.
-//   * Epilogue warps: tcgen05.ld the int32 partials, acc += P * (ws * as) in
-//     fp32 registers, bf16 store at the end of the tile.
+//   * Each K-group accumulates into its own int32 TMEM region.  Regions are
+//     handed to the epilogue through a ring of up to 8 accumulator slots (a
+//     slot holds one K-unit's groups when the token tile is small, else one
+//     group), so the MMA runs several groups ahead of the rescale instead of
+//     waiting for it.  For GK <= 256 a region is pre-set to the bits of
+//     1.5*2^23, so float(P) is one exact fp32 subtraction in the epilogue.
+//   * Epilogue warps: one batch of tcgen05.ld per slot, acc += P * (ws * as)
+//     with packed f32x2 arithmetic in registers, bf16 store at tile end.
 //   * Work split: stream-K over (tile, K-unit) so every SM gets the same number
 //     of weight bytes.  A tile split across CTAs is reduced deterministically
 //     by the last CTA to arrive (fixed summation order), which also resets the
@@ -54,9 +56,19 @@ struct Cfg {
     static constexpr int KPU = GK <= 256 ? 1 : GK / 256;     // k-blocks per unit (max)
     static constexpr bool SYM16 = !ASYM && GK <= 256;
     static constexpr bool MAGIC = GK <= 256;                 // magic-initialised accumulators
-    static constexpr int E = TT <= 64 ? 1 : 2;               // epilogue warpgroups
+    static constexpr int E = TT <= 32 ? 1 : 2;               // epilogue warpgroups
     static constexpr int NC = TT / E;                        // accumulator columns per thread
+    static constexpr int NCH = NC / 16;                      // 16-column TMEM chunks per thread
     static constexpr int THREADS = (kNumPreWarps + 4 * E) * 32;
+    // TMEM: 2 A buffers of 64 columns, the rest for accumulator slots.
+    static constexpr int ACC_COLS = 512 - kAccCol0;
+    // groups per accumulator slot: a whole unit when its columns fit one
+    // 32-register load batch of the epilogue and the ring stays >= 4 deep
+    static constexpr int CG = (GPK * NC <= 32 && ACC_COLS / (GPK * TT) >= 4) ? GPK : 1;
+    static constexpr int TOTCH = CG * NCH;                   // 16-column chunks per slot and thread
+    static constexpr int BCH = TOTCH < 2 ? TOTCH : 2;        // chunks per tcgen05.ld batch
+    static constexpr int NACC_FIT = ACC_COLS / (CG * TT);
+    static constexpr int NACC = NACC_FIT > 8 ? 8 : NACC_FIT;           // accumulator slots
     static constexpr int A_STAGE = TT * 256;
     static constexpr int STAGE = kWStageBytes + A_STAGE;
     __host__ __device__ static constexpr int r128(int x) { return (x + 127) / 128 * 128; }
@@ -64,20 +76,22 @@ struct Cfg {
     static constexpr int SL_WZ = ASYM ? GPK * 128 * 2 : 0;
     static constexpr int SL_AS = GPK * TT * 4;
     static constexpr int SLOT = r128(SL_WS) + r128(SL_WZ) + r128(SL_AS);
-    static constexpr int DS = 4;                             // scale slots
+    static constexpr int DS = TT <= 64 ? 8 : 4;              // scale slots
     static constexpr int S_FIT = (kSmemBudget - DS * SLOT - 1024) / STAGE;
     static constexpr int S = S_FIT > 8 ? 8 : S_FIT;          // pipeline stages
     static constexpr int BAR_OFF = S * STAGE + DS * SLOT;
     static constexpr int SMEM = BAR_OFF + 512 + 1024;        // + barriers + alignment slack
-    static constexpr int TMEM_COLS = (kAccCol0 + 2 * TT) <= 256 ? 256 : 512;
+    static constexpr int TMEM_COLS = 512;
     static_assert(S >= 3, "pipeline too shallow");
+    static_assert(NACC >= 2, "need at least two accumulator slots");
+    static_assert(NC % 16 == 0, "epilogue works in 16-column chunks");
 };
 
 struct Bars {
     uint64_t full[8], empty[8];
-    uint64_t sfull[4], sempty[4];
+    uint64_t sfull[8], sempty[8];
     uint64_t afull[2], aempty[2];
-    uint64_t accfull[2], accempty[2];
+    uint64_t accfull[8], accempty[8];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -145,6 +159,139 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads)
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// acc[j] += float(P_j) * (ws * as[j]) for NC consecutive columns, in packed
+// f32x2 arithmetic.  r holds the accumulator bits: 1.5*2^23 + P (MAGIC) or P.
+struct R16 {
+    uint32_t v[16];
+};
+
+// acc[16*i + j] += float(P_j) * (ws * as[j]) for one 16-column chunk.  The
+// accumulator lives in packed fp32 pairs (acc2[k] = columns 2k, 2k+1) so each
+// step is one f32x2 instruction on a register pair.  r holds the accumulator
+// bits: 1.5*2^23 + P (MAGIC) or P.
+template <int NC, bool MAGIC>
+__device__ __forceinline__ void rescale_chunk(uint64_t (&acc2)[NC / 2], int i, const R16& r, float wsv,
+                                              const float* asg)
+{
+    const uint64_t ws2 = pack2(wsv, wsv);
+    const uint64_t mg2 = pack2(kMagicF, kMagicF);
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(asg + j);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t r0 = r.v[j + 2 * h], r1 = r.v[j + 2 * h + 1];
+            uint64_t f2;
+            if (MAGIC) {
+                f2 = f2_sub(pack2u(r0, r1), mg2);
+            } else {
+                f2 = pack2(static_cast<float>(static_cast<int>(r0)), static_cast<float>(static_cast<int>(r1)));
+            }
+            const uint64_t c2 = f2_mul(ws2, h == 0 ? pack2(a4.x, a4.y) : pack2(a4.z, a4.w));
+            uint64_t& a = acc2[8 * i + j / 2 + h];
+            a = f2_fma(f2, c2, a);
+        }
+    }
+}
+
+__device__ __forceinline__ float acc_at(const uint64_t* acc2, int j)
+{
+    return __uint_as_float(static_cast<uint32_t>(acc2[j >> 1] >> ((j & 1) * 32)));
+}
+
+// The last CTA to finish a split tile sums the parts in contributor order
+// (16 columns at a time, up to four contributors' loads in flight) and stores
+// the bf16 tile.  Kept out of line so its registers do not add to the
+// epilogue's steady-state loop.
+template <int TT, int NC>
+__device__ __noinline__ void reduce_tile(const GemmParams& p, Unit un, int t, int cf, int cl, int nctas, int row,
+                                         int col0, int ew, int lane)
+{
+    __threadfence();
+    const int n = un.wt * 128 + row;
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
+    for (int cc = 0; cc < NC; cc += 16) {
+        float sum[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+        for (int c2 = cf; c2 <= cl; c2 += 4) {
+            float v[4][16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (c2 + q > cl) break;
+                int cu0, cu1;
+                cta_range(p, c2 + q, nctas, cu0, cu1);
+                const int s2 = (t == cu0 / p.units_per_tile) ? 0 : 1;
+                const float* src = p.partials + static_cast<int64_t>(2 * (c2 + q) + s2) * (TT * 128);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[q][j] = __ldcg(src + (col0 + cc + j) * 128 + row);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (c2 + q > cl) break;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sum[j] += v[q][j];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int m = un.tt * TT + col0 + cc + j;
+            if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
+        }
+    }
+    if (ew == 0 && lane == 0) p.counters[t] = 0;
+}
+
+// Debug output mode: the exact int32 partials of one 16-column chunk of group g.
+template <bool MAGIC, bool SYM16>
+__device__ __noinline__ void store_partials(const GemmParams& p, R16 r, int g, int m0, int n)
+{
+    if (n >= p.N) return;
+    int* dst = reinterpret_cast<int*>(p.out) + (static_cast<int64_t>(g) * p.M + m0) * p.N + n;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        int P = MAGIC ? static_cast<int>(r.v[j] - kMagicBits) : static_cast<int>(r.v[j]);
+        if (SYM16) P >>= 4;
+        if (m0 + j < p.M) dst[static_cast<int64_t>(j) * p.N] = P;
+    }
+}
+
+// End of a CTA's share of one output tile: store it, or hand the partial to the
+// stream-K reduction (the last CTA to arrive sums the parts in a fixed order).
+template <class C>
+__device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, int u0, int u1, int cta, int nctas,
+                                           int row, int col0, int ew, int lane, int nthr, const uint64_t (&acc2)[C::NC / 2],
+                                           Bars* bars)
+{
+    constexpr int TT = C::TT, NC = C::NC;
+    const int t = un.t;
+    const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
+    const int n = un.wt * 128 + row;
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
+    if (u0 <= tfirst && u1 - 1 >= tlast) {
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+            const int m = un.tt * TT + col0 + j;
+            if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(acc_at(acc2, j));
+        }
+        return;
+    }
+    const int side = (t == u0 / p.units_per_tile) ? 0 : 1;
+    float* mine = p.partials + static_cast<int64_t>(2 * cta + side) * (TT * 128);
+#pragma unroll
+    for (int j = 0; j < NC; ++j) mine[(col0 + j) * 128 + row] = acc_at(acc2, j);
+    __threadfence();
+    named_bar_sync(1, nthr);
+    const int cf = cta_of_unit(p, tfirst, nctas), cl = cta_of_unit(p, tlast, nctas);
+    if (ew == 0 && lane == 0) {
+        const int old = atomicAdd(&p.counters[t], 1);
+        bars->last_flag = (old == cl - cf) ? 1 : 0;
+    }
+    named_bar_sync(1, nthr);
+    if (bars->last_flag) reduce_tile<TT, NC>(p, un, t, cf, cl, nctas, row, col0, ew, lane);
+    named_bar_sync(1, nthr);   // last_flag is reused by the next tile
+}
+
 template <int TT, int GK, bool ASYM>
 __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     w4a8_gemm_kernel(const __grid_constant__ GemmParams p, const int ws_bf16, const int out_partials)
@@ -180,6 +327,8 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->afull[i], 4);
             mbar_init(&bars->aempty[i], 1);
+        }
+        for (int i = 0; i < C::NACC; ++i) {
             mbar_init(&bars->accfull[i], 1);
             mbar_init(&bars->accempty[i], 4 * C::E);
         }
@@ -212,9 +361,9 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             if (C::ASYM) tma_prefetch_desc(&p.tm_wz);
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_a = policy_evict_last();
-            int last_par[8], slot_par[4];
+            int last_par[8], slot_par[8];
             for (int i = 0; i < 8; ++i) last_par[i] = -1;
-            for (int i = 0; i < 4; ++i) slot_par[i] = -1;
+            for (int i = 0; i < 8; ++i) slot_par[i] = -1;
             bool ok = true;
 
             // Walk state: (u, kbi) -> stage / slot indices.
@@ -310,8 +459,8 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         // ============================================================ MMA issuer
         if (elect_one()) {
             const uint32_t idesc = idesc_i8(128, TT);
-            int stage = 0, ab = 0, accb = 0;
-            uint32_t sph = 0, abph = 0, accph = 0;
+            int stage = 0, ab = 0, sl = 0;
+            uint32_t sph = 0, abph = 0, slph = 0;
             bool ok = true;
             for (int u = u0; ok && u < u1; ++u) {
                 const Unit un = unit_of(p, u);
@@ -326,9 +475,12 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                     const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * 64);
                     if (C::GK <= 256) {
                         for (int g = g0; g < g1; ++g) {
-                            if (!mbar_wait(&bars->accempty[accb], accph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
-                            tc_fence_after();
-                            const uint32_t d_tmem = tbase + kAccCol0 + static_cast<uint32_t>(accb * TT);
+                            if (C::CG == 1 || g == g0) {
+                                if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                                tc_fence_after();
+                            }
+                            const uint32_t d_tmem = tbase + kAccCol0 +
+                                static_cast<uint32_t>(sl * C::CG * TT + (C::CG == 1 ? 0 : (g - g0) * TT));
                             const int ks0 = (g - g0) * (C::GK / 32);
 #pragma unroll
                             for (int j = 0; j < C::GK / 32; ++j) {
@@ -336,25 +488,27 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                                 const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
                                 tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, 1u);
                             }
-                            tc_commit(&bars->accfull[accb]);
-                            if (++accb == 2) { accb = 0; accph ^= 1; }
+                            if (C::CG == 1 || g == g1 - 1) {
+                                tc_commit(&bars->accfull[sl]);
+                                if (++sl == C::NACC) { sl = 0; slph ^= 1; }
+                            }
                         }
                         if (!ok) break;
                     } else {
                         const bool first = (kbg == kb0), last = (kbg == kb1 - 1);
                         if (first) {
-                            if (!mbar_wait(&bars->accempty[accb], accph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                            if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                             tc_fence_after();
                         }
-                        const uint32_t d_tmem = tbase + kAccCol0 + static_cast<uint32_t>(accb * TT);
+                        const uint32_t d_tmem = tbase + kAccCol0 + static_cast<uint32_t>(sl * TT);
 #pragma unroll
                         for (int ks = 0; ks < 8; ++ks) {
                             const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
                             tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, (first && ks == 0) ? 0u : 1u);
                         }
                         if (last) {
-                            tc_commit(&bars->accfull[accb]);
-                            if (++accb == 2) { accb = 0; accph ^= 1; }
+                            tc_commit(&bars->accfull[sl]);
+                            if (++sl == C::NACC) { sl = 0; slph ^= 1; }
                         }
                     }
                     tc_commit(&bars->aempty[ab]);
@@ -437,33 +591,33 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         // ============================================================ epilogue
         const int ew = warp - kNumPreWarps;
         const int quarter = warp & 3;
-        const int half = ew >> 2;
+        const int part = ew >> 2;
         const int row = quarter * 32 + lane;
-        const int col0 = half * C::NC;
+        const int col0 = part * C::NC;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        constexpr int NCH = C::NC / 16;
+        constexpr int NCH = C::NCH;
         const int nthr = 4 * C::E * 32;
 
         if (C::MAGIC) {
+            for (int b = 0; b < C::NACC; ++b)
 #pragma unroll
-            for (int b = 0; b < 2; ++b)
+                for (int gi = 0; gi < C::CG; ++gi)
 #pragma unroll
-                for (int i = 0; i < NCH; ++i)
-                    tc_st16_fill(tbase + lane_off + kAccCol0 + b * TT + col0 + 16 * i, kMagicBits);
+                    for (int i = 0; i < NCH; ++i)
+                        tc_st16_fill(tbase + lane_off + kAccCol0 + (b * C::CG + gi) * TT + col0 + 16 * i, kMagicBits);
             tc_wait_st();
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&bars->accempty[0]);
-            mbar_arrive(&bars->accempty[1]);
-        }
+        if (lane == 0)
+            for (int b = 0; b < C::NACC; ++b) mbar_arrive(&bars->accempty[b]);
+        __syncwarp();
 
-        float acc[C::NC];
+        uint64_t acc2[C::NC / 2];
 #pragma unroll
-        for (int j = 0; j < C::NC; ++j) acc[j] = 0.0f;
-        int slot = 0, accb = 0;
-        uint32_t slph = 0, accph = 0;
+        for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
+        int slot = 0, sl = 0;
+        uint32_t slph = 0, aph = 0;
         bool ok = true;
         for (int u = u0; ok && u < u1; ++u) {
             const Unit un = unit_of(p, u);
@@ -472,109 +626,61 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             if (!warp_wait(&bars->sfull[slot], slph, abort_flag, p.status, kWEpiSlot)) { ok = false; break; }
             const uint8_t* wsb = slot_ws(slot);
             const float* asb = slot_as(slot);
-            for (int g = g0; g < g1; ++g) {
-                const int gi = g - g0;
-                float wsv = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gi * 128 + row])
-                                    : reinterpret_cast<const float*>(wsb)[gi * 128 + row];
-                if (C::SYM16) wsv *= 0.0625f;   // the unpack carried weights as 16*w
-                if (!warp_wait(&bars->accfull[accb], accph, abort_flag, p.status, kWEpiAccFull)) { ok = false; break; }
+            // one accumulator slot holds CG groups: all of this unit's, or one
+            for (int gs = g0; gs < g1; gs += C::CG) {
+                if (!warp_wait(&bars->accfull[sl], aph, abort_flag, p.status, kWEpiAccFull)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t t_acc = tbase + lane_off + kAccCol0 + static_cast<uint32_t>(accb * TT + col0);
-                const float* asg = asb + gi * TT + col0;
+                const uint32_t t_slot = tbase + lane_off + kAccCol0 + static_cast<uint32_t>(sl * C::CG * TT + col0);
 #pragma unroll
-                for (int i = 0; i < NCH; ++i) {
-                    uint32_t r[16];
-                    tc_ld16(t_acc + 16 * i, r);
+                for (int b0 = 0; b0 < C::TOTCH; b0 += C::BCH) {
+                    R16 r[C::BCH];
+#pragma unroll
+                    for (int q = 0; q < C::BCH; ++q) {
+                        const int c = b0 + q;
+                        tc_ld16(t_slot + (c / NCH) * TT + 16 * (c % NCH), r[q].v);
+                    }
                     tc_wait_ld();
-                    if (C::MAGIC) tc_st16_fill(t_acc + 16 * i, kMagicBits);
-                    if (!out_partials) {
+                    if (C::MAGIC) {
 #pragma unroll
-                        for (int j4 = 0; j4 < 4; ++j4) {
-                            const float4 a4 = *reinterpret_cast<const float4*>(asg + 16 * i + 4 * j4);
-                            const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-#pragma unroll
-                            for (int jj = 0; jj < 4; ++jj) {
-                                const int j = 4 * j4 + jj;
-                                const float f = C::MAGIC ? (__uint_as_float(r[j]) - kMagicF)
-                                                         : static_cast<float>(static_cast<int>(r[j]));
-                                acc[16 * i + j] = fmaf(f, wsv * av[jj], acc[16 * i + j]);
-                            }
+                        for (int q = 0; q < C::BCH; ++q) {
+                            const int c = b0 + q;
+                            tc_st16_fill(t_slot + (c / NCH) * TT + 16 * (c % NCH), kMagicBits);
                         }
-                    } else {
-                        const int n = un.wt * 128 + row;
+                    }
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const int m = un.tt * TT + col0 + 16 * i + j;
-                            int P = C::MAGIC ? static_cast<int>(r[j] - kMagicBits) : static_cast<int>(r[j]);
-                            if (C::SYM16) P >>= 4;
-                            if (m < p.M && n < p.N)
-                                reinterpret_cast<int*>(p.out)[(static_cast<int64_t>(g) * p.M + m) * p.N + n] = P;
+                    for (int q = 0; q < C::BCH; ++q) {
+                        const int c = b0 + q, gi = c / NCH, i = c % NCH;
+                        const int g = gs + gi;
+                        if (g >= g1) continue;
+                        const int gl = g - g0;           // group index within the unit's scale slot
+                        if (!out_partials) {
+                            float wsv = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gl * 128 + row])
+                                                : reinterpret_cast<const float*>(wsb)[gl * 128 + row];
+                            if (C::SYM16) wsv *= 0.0625f;   // the unpack carried weights as 16*w
+                            rescale_chunk<C::NC, C::MAGIC>(acc2, i, r[q], wsv, asb + gl * TT + col0 + 16 * i);
+                        } else {
+                            store_partials<C::MAGIC, C::SYM16>(p, r[q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
                         }
                     }
                 }
                 if (C::MAGIC) tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->accempty[accb]);
+                if (lane == 0) mbar_arrive(&bars->accempty[sl]);
                 __syncwarp();
-                if (++accb == 2) { accb = 0; accph ^= 1; }
+                if (++sl == C::NACC) { sl = 0; aph ^= 1; }
             }
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->sempty[slot]);
+            __syncwarp();
             if (++slot == C::DS) { slot = 0; slph ^= 1; }
 
             // ---- end of this CTA's share of tile t: store or hand over ----
             if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
-                if (!out_partials) {
-                    const int t = un.t;
-                    const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
-                    const int n = un.wt * 128 + row;
-                    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
-                    if (u0 <= tfirst && u1 - 1 >= tlast) {
+                if (!out_partials) flush_tile<C>(p, un, u0, u1, cta, nctas, row, col0, ew, lane, nthr, acc2, bars);
 #pragma unroll
-                        for (int j = 0; j < C::NC; ++j) {
-                            const int m = un.tt * TT + col0 + j;
-                            if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(acc[j]);
-                        }
-                    } else {
-                        const int side = (t == u0 / p.units_per_tile) ? 0 : 1;
-                        float* mine = p.partials + static_cast<int64_t>(2 * cta + side) * (TT * 128);
-#pragma unroll
-                        for (int j = 0; j < C::NC; ++j) mine[(col0 + j) * 128 + row] = acc[j];
-                        __threadfence();
-                        named_bar_sync(1, nthr);
-                        const int cf = cta_of_unit(p, tfirst, nctas), cl = cta_of_unit(p, tlast, nctas);
-                        if (ew == 0 && lane == 0) {
-                            const int old = atomicAdd(&p.counters[t], 1);
-                            bars->last_flag = (old == cl - cf) ? 1 : 0;
-                        }
-                        named_bar_sync(1, nthr);
-                        if (bars->last_flag) {
-                            __threadfence();
-                            float sum[C::NC];
-#pragma unroll
-                            for (int j = 0; j < C::NC; ++j) sum[j] = 0.0f;
-                            for (int c2 = cf; c2 <= cl; ++c2) {
-                                int cu0, cu1;
-                                cta_range(p, c2, nctas, cu0, cu1);
-                                const int s2 = (t == cu0 / p.units_per_tile) ? 0 : 1;
-                                const float* src = p.partials + static_cast<int64_t>(2 * c2 + s2) * (TT * 128);
-#pragma unroll
-                                for (int j = 0; j < C::NC; ++j) sum[j] += __ldcg(src + (col0 + j) * 128 + row);
-                            }
-#pragma unroll
-                            for (int j = 0; j < C::NC; ++j) {
-                                const int m = un.tt * TT + col0 + j;
-                                if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
-                            }
-                            if (ew == 0 && lane == 0) p.counters[t] = 0;
-                        }
-                        named_bar_sync(1, nthr);   // last_flag is reused by the next tile
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < C::NC; ++j) acc[j] = 0.0f;
+                for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
             }
         }
     }
