@@ -156,32 +156,108 @@ int run_quant_kernel_layout(const Plan& pl, const void* x, int64_t ldx, uint8_t*
     return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
 }
 
+// Encoded descriptors of one (weights, workspace, shape) combination.  Encoding
+// five tensor maps costs microseconds of host time per call, so recently used
+// sets are kept (a serving loop calls the same few layers over and over).
+struct MapKey {
+    const void* w_packed;
+    const void* w_scale;
+    const void* w_zero;
+    const void* ws;
+    int64_t M, N, K;
+    int gk, ws_dtype, partials, dev;
+    bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+
+struct MapEntry {
+    MapKey key;
+    CUtensorMap maps[5];
+    uint64_t stamp;
+    bool used;
+};
+
+constexpr int kMapCache = 128;
+MapEntry g_maps[kMapCache];
+uint64_t g_map_clock = 0;
+std::mutex g_map_mutex;
+
+bool encode_maps(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
+                 bool partials, uint8_t* ws, CUtensorMap* m)
+{
+    const int gpk = pl.gk <= 256 ? 256 / pl.gk : 1;
+    return encode_2d(&m[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, w_packed, pl.Kpad / 2, pl.N, pl.Kpad / 2, 128, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_2d(&m[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, ws + pl.off_aq, pl.Kpad, pl.M, pl.Kpad, 128, pl.tt,
+                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+           (partials
+                // scales are not read in this mode: describe a small region the workspace owns
+                ? encode_2d(&m[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.as_ld, pl.G, pl.as_ld * 4,
+                            128, gpk, CU_TENSOR_MAP_SWIZZLE_NONE)
+                : encode_2d(&m[2],
+                            ws_dtype == W4A8_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                            w_scale, pl.N, pl.G, pl.N * (ws_dtype == W4A8_DTYPE_F32 ? 4 : 2), 128, gpk,
+                            CU_TENSOR_MAP_SWIZZLE_NONE)) &&
+           (w_zero == nullptr ||
+            encode_2d(&m[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, w_zero, pl.N, pl.G, pl.N * 2, 128, gpk,
+                      CU_TENSOR_MAP_SWIZZLE_NONE)) &&
+           encode_2d(&m[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.M, pl.G, pl.as_ld * 4, pl.tt, gpk,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+bool cached_maps(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
+                 bool partials, uint8_t* ws, GemmParams& g)
+{
+    MapKey k;
+    std::memset(&k, 0, sizeof(k));
+    k.w_packed = w_packed;
+    k.w_scale = w_scale;
+    k.w_zero = w_zero;
+    k.ws = ws;
+    k.M = pl.M;
+    k.N = pl.N;
+    k.K = pl.K;
+    k.gk = pl.gk;
+    k.ws_dtype = ws_dtype;
+    k.partials = partials ? 1 : 0;
+    cudaGetDevice(&k.dev);
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    int victim = 0;
+    for (int i = 0; i < kMapCache; ++i) {
+        if (g_maps[i].used && g_maps[i].key == k) {
+            g_maps[i].stamp = ++g_map_clock;
+            std::memcpy(&g.tm_w, &g_maps[i].maps[0], sizeof(CUtensorMap));
+            std::memcpy(&g.tm_a, &g_maps[i].maps[1], sizeof(CUtensorMap));
+            std::memcpy(&g.tm_ws, &g_maps[i].maps[2], sizeof(CUtensorMap));
+            std::memcpy(&g.tm_wz, &g_maps[i].maps[3], sizeof(CUtensorMap));
+            std::memcpy(&g.tm_as, &g_maps[i].maps[4], sizeof(CUtensorMap));
+            return true;
+        }
+        if (g_maps[victim].used && (!g_maps[i].used || g_maps[i].stamp < g_maps[victim].stamp)) victim = i;
+    }
+    MapEntry& e = g_maps[victim];
+    std::memset(e.maps, 0, sizeof(e.maps));
+    if (!encode_maps(pl, w_packed, w_scale, ws_dtype, w_zero, partials, ws, e.maps)) {
+        e.used = false;
+        return false;
+    }
+    e.key = k;
+    e.used = true;
+    e.stamp = ++g_map_clock;
+    std::memcpy(&g.tm_w, &e.maps[0], sizeof(CUtensorMap));
+    std::memcpy(&g.tm_a, &e.maps[1], sizeof(CUtensorMap));
+    std::memcpy(&g.tm_ws, &e.maps[2], sizeof(CUtensorMap));
+    std::memcpy(&g.tm_wz, &e.maps[3], sizeof(CUtensorMap));
+    std::memcpy(&g.tm_as, &e.maps[4], sizeof(CUtensorMap));
+    return true;
+}
+
 int run_gemm(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
              void* out, int64_t ldy, bool partials, uint8_t* ws, cudaStream_t st)
 {
     if (get_encoder() != W4A8_OK) return fail_cuda(cudaErrorNotSupported);
     GemmParams g;
     std::memset(&g, 0, sizeof(g));
-    const int gpk = pl.gk <= 256 ? 256 / pl.gk : 1;
-    const bool ok =
-        encode_2d(&g.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_packed, pl.Kpad / 2, pl.N, pl.Kpad / 2, 128, 128,
-                  CU_TENSOR_MAP_SWIZZLE_128B) &&
-        encode_2d(&g.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, ws + pl.off_aq, pl.Kpad, pl.M, pl.Kpad, 128, pl.tt,
-                  CU_TENSOR_MAP_SWIZZLE_128B) &&
-        (partials
-             // scales are not read in this mode: describe a small region the workspace owns
-             ? encode_2d(&g.tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.as_ld, pl.G, pl.as_ld * 4,
-                         128, gpk, CU_TENSOR_MAP_SWIZZLE_NONE)
-             : encode_2d(&g.tm_ws,
-                         ws_dtype == W4A8_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                         w_scale, pl.N, pl.G, pl.N * (ws_dtype == W4A8_DTYPE_F32 ? 4 : 2), 128, gpk,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)) &&
-        (w_zero == nullptr ||
-         encode_2d(&g.tm_wz, CU_TENSOR_MAP_DATA_TYPE_UINT16, w_zero, pl.N, pl.G, pl.N * 2, 128, gpk,
-                   CU_TENSOR_MAP_SWIZZLE_NONE)) &&
-        encode_2d(&g.tm_as, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.M, pl.G, pl.as_ld * 4, pl.tt, gpk,
-                  CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (!ok) return W4A8_ERR_INVALID;
+    if (!cached_maps(pl, w_packed, w_scale, ws_dtype, w_zero, partials, ws, g)) return W4A8_ERR_INVALID;
     g.out = out;
     g.partials = reinterpret_cast<float*>(ws + pl.off_part);
     g.counters = reinterpret_cast<int*>(ws + pl.off_counters);

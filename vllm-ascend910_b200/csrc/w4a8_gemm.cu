@@ -39,8 +39,8 @@ namespace w4a8 {
 namespace {
 
 constexpr int kWStageBytes = 128 * 128;   // 128 weight rows x 128 B (256 int4)
-constexpr int kNumPreWarps = 6;           // producer, MMA, 4 converters
-constexpr int kAccCol0 = 128;             // TMEM: A buffers in [0,128), accumulators after
+constexpr int kNumPreWarps = 7;           // producer, 2 MMA issuers, 4 converters
+constexpr int kNumIssuers = 2;            // one thread issues a tcgen05.mma every ~80 cycles: use two
 constexpr int kSmemBudget = 227 * 1024 - 1024;
 
 // wait-site ids for the status word
@@ -60,8 +60,11 @@ struct Cfg {
     static constexpr int NC = TT / E;                        // accumulator columns per thread
     static constexpr int NCH = NC / 16;                      // 16-column TMEM chunks per thread
     static constexpr int THREADS = (kNumPreWarps + 4 * E) * 32;
-    // TMEM: 2 A buffers of 64 columns, the rest for accumulator slots.
-    static constexpr int ACC_COLS = 512 - kAccCol0;
+    // TMEM: NA A buffers of 64 columns (one k-block of int8 weights), the rest
+    // for accumulator slots.
+    static constexpr int NA = TT <= 64 ? 4 : 2;
+    static constexpr int ACC0 = NA * 64;
+    static constexpr int ACC_COLS = 512 - ACC0;
     // groups per accumulator slot: a whole unit when its columns fit one
     // 32-register load batch of the epilogue and the ring stays >= 4 deep
     static constexpr int CG = (GPK * NC <= 32 && ACC_COLS / (GPK * TT) >= 4) ? GPK : 1;
@@ -90,9 +93,9 @@ struct Cfg {
 struct Bars {
     uint64_t full[8], empty[8];
     uint64_t sfull[8], sempty[8];
-    uint64_t afull[2], aempty[2];
+    uint64_t afull[4], aempty[4];
     uint64_t accfull[8], accempty[8];
-    uint64_t drain;
+    uint64_t drain[2];
     uint32_t tmem_base;
     int abort;
     int last_flag;
@@ -318,21 +321,22 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::S; ++i) {
             mbar_init(&bars->full[i], 1);
-            mbar_init(&bars->empty[i], 4 + 1);          // 4 converter warps + MMA commit
+            mbar_init(&bars->empty[i], 4 + kNumIssuers);  // 4 converter warps + each issuer's commit
         }
         for (int i = 0; i < C::DS; ++i) {
             mbar_init(&bars->sfull[i], 1);
             mbar_init(&bars->sempty[i], 4 + 4 * C::E);  // converter + epilogue warps
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < C::NA; ++i) {
             mbar_init(&bars->afull[i], 4);
-            mbar_init(&bars->aempty[i], 1);
+            mbar_init(&bars->aempty[i], kNumIssuers);
         }
         for (int i = 0; i < C::NACC; ++i) {
             mbar_init(&bars->accfull[i], 1);
             mbar_init(&bars->accempty[i], 4 * C::E);
         }
-        mbar_init(&bars->drain, 1);
+        mbar_init(&bars->drain[0], 1);
+        mbar_init(&bars->drain[1], 1);
         bars->abort = 0;
         fence_mbar_init();
     }
@@ -455,11 +459,15 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             for (int i = 0; i < C::DS; ++i)
                 if (slot_par[i] >= 0) mbar_wait(&bars->sfull[i], static_cast<uint32_t>(slot_par[i]), abort_flag, p.status, kWDrain);
         }
-    } else if (warp == 1) {
-        // ============================================================ MMA issuer
+    } else if (warp <= kNumIssuers) {
+        // ============================================================ MMA issuers
+        // Both issuers walk every k-block; issuer i issues the MMAs of the
+        // accumulator slots whose global index is i mod 2, and both commit the
+        // k-block's A buffer and stage back (each covering its own MMAs).
+        const int me = warp - 1;
         if (elect_one()) {
             const uint32_t idesc = idesc_i8(128, TT);
-            int stage = 0, ab = 0, sl = 0;
+            int stage = 0, ab = 0, sl = 0, gsl = 0;
             uint32_t sph = 0, abph = 0, slph = 0;
             bool ok = true;
             for (int u = u0; ok && u < u1; ++u) {
@@ -475,51 +483,59 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                     const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * 64);
                     if (C::GK <= 256) {
                         for (int g = g0; g < g1; ++g) {
-                            if (C::CG == 1 || g == g0) {
+                            const bool mine = (gsl & 1) == me;
+                            if (mine && (C::CG == 1 || g == g0)) {
                                 if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                                 tc_fence_after();
                             }
-                            const uint32_t d_tmem = tbase + kAccCol0 +
-                                static_cast<uint32_t>(sl * C::CG * TT + (C::CG == 1 ? 0 : (g - g0) * TT));
-                            const int ks0 = (g - g0) * (C::GK / 32);
+                            if (mine) {
+                                const uint32_t d_tmem = tbase + C::ACC0 +
+                                    static_cast<uint32_t>(sl * C::CG * TT + (C::CG == 1 ? 0 : (g - g0) * TT));
+                                const int ks0 = (g - g0) * (C::GK / 32);
 #pragma unroll
-                            for (int j = 0; j < C::GK / 32; ++j) {
-                                const int ks = ks0 + j;
-                                const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
-                                tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, 1u);
+                                for (int j = 0; j < C::GK / 32; ++j) {
+                                    const int ks = ks0 + j;
+                                    const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
+                                    tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, 1u);
+                                }
                             }
                             if (C::CG == 1 || g == g1 - 1) {
-                                tc_commit(&bars->accfull[sl]);
+                                if (mine) tc_commit(&bars->accfull[sl]);
+                                ++gsl;
                                 if (++sl == C::NACC) { sl = 0; slph ^= 1; }
                             }
                         }
                         if (!ok) break;
                     } else {
                         const bool first = (kbg == kb0), last = (kbg == kb1 - 1);
-                        if (first) {
-                            if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
-                            tc_fence_after();
-                        }
-                        const uint32_t d_tmem = tbase + kAccCol0 + static_cast<uint32_t>(sl * TT);
+                        const bool mine = (gsl & 1) == me;
+                        if (mine) {
+                            if (first) {
+                                if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                                tc_fence_after();
+                            }
+                            const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>(sl * TT);
 #pragma unroll
-                        for (int ks = 0; ks < 8; ++ks) {
-                            const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
-                            tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, (first && ks == 0) ? 0u : 1u);
+                            for (int ks = 0; ks < 8; ++ks) {
+                                const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
+                                tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, (first && ks == 0) ? 0u : 1u);
+                            }
+                            if (last) tc_commit(&bars->accfull[sl]);
                         }
                         if (last) {
-                            tc_commit(&bars->accfull[sl]);
+                            ++gsl;
                             if (++sl == C::NACC) { sl = 0; slph ^= 1; }
                         }
                     }
                     tc_commit(&bars->aempty[ab]);
                     tc_commit(&bars->empty[stage]);
-                    if (++ab == 2) { ab = 0; abph ^= 1; }
+                    if (++ab == C::NA) { ab = 0; abph ^= 1; }
                     if (++stage == C::S) { stage = 0; sph ^= 1; }
                 }
             }
             // Wait for every MMA issued by this thread before TMEM can be released.
-            tc_commit(&bars->drain);
-            mbar_wait(&bars->drain, 0, abort_flag, p.status, kWDrain);
+            tc_commit(&bars->drain[me]);
+            mbar_wait(&bars->drain[me], 0, abort_flag, p.status, kWDrain);
         }
     } else if (warp < kNumPreWarps) {
         // ============================================================ converters
@@ -579,7 +595,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                     mbar_arrive(&bars->empty[stage]);
                 }
                 __syncwarp();
-                if (++ab == 2) { ab = 0; abph ^= 1; }
+                if (++ab == C::NA) { ab = 0; abph ^= 1; }
                 if (++stage == C::S) { stage = 0; sph ^= 1; }
             }
             if (!ok) break;
@@ -604,7 +620,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 for (int gi = 0; gi < C::CG; ++gi)
 #pragma unroll
                     for (int i = 0; i < NCH; ++i)
-                        tc_st16_fill(tbase + lane_off + kAccCol0 + (b * C::CG + gi) * TT + col0 + 16 * i, kMagicBits);
+                        tc_st16_fill(tbase + lane_off + C::ACC0 + (b * C::CG + gi) * TT + col0 + 16 * i, kMagicBits);
             tc_wait_st();
         }
         tc_fence_before();
@@ -630,7 +646,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             for (int gs = g0; gs < g1; gs += C::CG) {
                 if (!warp_wait(&bars->accfull[sl], aph, abort_flag, p.status, kWEpiAccFull)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t t_slot = tbase + lane_off + kAccCol0 + static_cast<uint32_t>(sl * C::CG * TT + col0);
+                const uint32_t t_slot = tbase + lane_off + C::ACC0 + static_cast<uint32_t>(sl * C::CG * TT + col0);
 #pragma unroll
                 for (int b0 = 0; b0 < C::TOTCH; b0 += C::BCH) {
                     R16 r[C::BCH];
@@ -700,8 +716,16 @@ cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pd
 {
     using C = Cfg<TT, GK, ASYM>;
     auto kern = w4a8_gemm_kernel<TT, GK, ASYM>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    // The shared-memory opt-in is per device; set it once per device.
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_done[dev] = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(C::THREADS);
