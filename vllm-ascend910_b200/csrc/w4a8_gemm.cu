@@ -39,7 +39,8 @@ namespace w4a8 {
 namespace {
 
 constexpr int kWStageBytes = 128 * 128;   // 128 weight rows x 128 B (256 int4)
-constexpr int kNumPreWarps = 7;           // producer, 2 MMA issuers, 4 converters
+constexpr int kNumPreWarps = 8;           // weight producer, 2 MMA issuers, activation producer, 4 converters
+constexpr int kActProducerWarp = 3;
 constexpr int kNumIssuers = 2;            // one thread issues a tcgen05.mma every ~80 cycles: use two
 constexpr int kSmemBudget = 227 * 1024 - 1024;
 
@@ -80,10 +81,10 @@ struct Cfg {
     static constexpr int SL_AS = GPK * TT * 4;
     static constexpr int SLOT = r128(SL_WS) + r128(SL_WZ) + r128(SL_AS);
     static constexpr int DS = TT <= 64 ? 8 : 4;              // scale slots
-    static constexpr int S_FIT = (kSmemBudget - DS * SLOT - 1024) / STAGE;
-    static constexpr int S = S_FIT > 8 ? 8 : S_FIT;          // pipeline stages
+    static constexpr int S_FIT = (kSmemBudget - DS * SLOT - 2048) / STAGE;
+    static constexpr int S = S_FIT > 12 ? 12 : S_FIT;        // pipeline stages
     static constexpr int BAR_OFF = S * STAGE + DS * SLOT;
-    static constexpr int SMEM = BAR_OFF + 512 + 1024;        // + barriers + alignment slack
+    static constexpr int SMEM = BAR_OFF + 1024 + 1024;       // + barriers + alignment slack
     static constexpr int TMEM_COLS = 512;
     static_assert(S >= 3, "pipeline too shallow");
     static_assert(NACC >= 2, "need at least two accumulator slots");
@@ -91,7 +92,7 @@ struct Cfg {
 };
 
 struct Bars {
-    uint64_t full[8], empty[8];
+    uint64_t full[12], empty[12];
     uint64_t sfull[8], sempty[8];
     uint64_t afull[4], aempty[4];
     uint64_t accfull[8], accempty[8];
@@ -101,7 +102,8 @@ struct Bars {
     int last_flag;
 };
 
-static_assert(sizeof(Bars) <= 512, "barrier block overflows its reservation");
+static_assert(sizeof(Bars) <= 1024, "barrier block overflows its reservation");
+static_assert(Cfg<16, 128, false>::S <= 12, "stage barriers");
 
 struct Unit {
     int t, wt, tt, ut;
@@ -210,7 +212,6 @@ template <int TT, int NC>
 __device__ __noinline__ void reduce_tile(const GemmParams& p, Unit un, int t, int cf, int cl, int nctas, int row,
                                          int col0, int ew, int lane)
 {
-    __threadfence();
     const int n = un.wt * 128 + row;
     __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
     for (int cc = 0; cc < NC; cc += 16) {
@@ -259,12 +260,29 @@ __device__ __noinline__ void store_partials(const GemmParams& p, R16 r, int g, i
     }
 }
 
-// End of a CTA's share of one output tile: store it, or hand the partial to the
-// stream-K reduction (the last CTA to arrive sums the parts in a fixed order).
+// A split tile this CTA contributed to, remembered until the end of the CTA's
+// range, when the arrival count returned by its release/acquire atomic says
+// whether this CTA was the last contributor (and so reduces the tile).
+struct Pending {
+    Unit un;
+    int cf, cl;
+    int old;     // arrival count before this CTA's arrival (meaningful in the electing thread)
+    int valid;
+};
+
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v)
+{
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+
+// End of a CTA's share of one output tile: store it, or store the partial and
+// announce it with one release/acquire atomic whose answer is consumed later.
 template <class C>
 __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, int u0, int u1, int cta, int nctas,
-                                           int row, int col0, int ew, int lane, int nthr, const uint64_t (&acc2)[C::NC / 2],
-                                           Bars* bars)
+                                           int row, int col0, int ew, int lane, int nthr,
+                                           const uint64_t (&acc2)[C::NC / 2], Pending& pend)
 {
     constexpr int TT = C::TT, NC = C::NC;
     const int t = un.t;
@@ -282,17 +300,35 @@ __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, 
     const int side = (t == u0 / p.units_per_tile) ? 0 : 1;
     float* mine = p.partials + static_cast<int64_t>(2 * cta + side) * (TT * 128);
 #pragma unroll
-    for (int j = 0; j < NC; ++j) mine[(col0 + j) * 128 + row] = acc_at(acc2, j);
-    __threadfence();
-    named_bar_sync(1, nthr);
-    const int cf = cta_of_unit(p, tfirst, nctas), cl = cta_of_unit(p, tlast, nctas);
+    for (int j = 0; j < NC; ++j) __stcg(mine + (col0 + j) * 128 + row, acc_at(acc2, j));
+    named_bar_sync(1, nthr);     // every epilogue thread's part is written (CTA-scope order)
+    pend.un = un;
+    pend.cf = cta_of_unit(p, tfirst, nctas);
+    pend.cl = cta_of_unit(p, tlast, nctas);
+    pend.valid = 1;
+    // Release (cumulative over the barrier above) publishes the part; acquire
+    // lets a last arriver see every other part.  The result is only read at
+    // the end of the CTA, so the round trip overlaps the rest of the work.
+    if (ew == 0 && lane == 0) pend.old = atom_add_acq_rel_gpu(&p.counters[t], 1);
+}
+
+// After the CTA's last unit: reduce the split tiles this CTA arrived last at.
+template <class C>
+__device__ __forceinline__ void finish_pending(const GemmParams& p, int nctas, int row, int col0, int ew, int lane,
+                                               int nthr, Pending (&pend)[2], Bars* bars)
+{
     if (ew == 0 && lane == 0) {
-        const int old = atomicAdd(&p.counters[t], 1);
-        bars->last_flag = (old == cl - cf) ? 1 : 0;
+        bars->last_flag = 0;
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+            if (pend[i].valid && pend[i].old == pend[i].cl - pend[i].cf) bars->last_flag |= 1 << i;
     }
     named_bar_sync(1, nthr);
-    if (bars->last_flag) reduce_tile<TT, NC>(p, un, t, cf, cl, nctas, row, col0, ew, lane);
-    named_bar_sync(1, nthr);   // last_flag is reused by the next tile
+    const int flags = bars->last_flag;
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        if (flags & (1 << i))
+            reduce_tile<C::TT, C::NC>(p, pend[i].un, pend[i].un.t, pend[i].cf, pend[i].cl, nctas, row, col0, ew, lane);
 }
 
 template <int TT, int GK, bool ASYM>
@@ -320,11 +356,11 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     // ---------------------------------------------------------------- setup
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::S; ++i) {
-            mbar_init(&bars->full[i], 1);
+            mbar_init(&bars->full[i], 2);               // weight and activation producers
             mbar_init(&bars->empty[i], 4 + kNumIssuers);  // 4 converter warps + each issuer's commit
         }
         for (int i = 0; i < C::DS; ++i) {
-            mbar_init(&bars->sfull[i], 1);
+            mbar_init(&bars->sfull[i], 2);
             mbar_init(&bars->sempty[i], 4 + 4 * C::E);  // converter + epilogue warps
         }
         for (int i = 0; i < C::NA; ++i) {
@@ -352,106 +388,63 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     pdl_launch_dependents();
 
     const uint32_t ws_elt = ws_bf16 ? 2u : 4u;
-    const uint32_t slot_tx = static_cast<uint32_t>(C::GPK * 128) * ws_elt +
-                             (C::ASYM ? C::GPK * 128 * 2 : 0) + C::GPK * C::TT * 4;
 
-    if (warp == 0) {
-        // ============================================================ producer
+    if (warp == 0 || warp == kActProducerWarp) {
+        // ============================================================ producers
+        // Warp 0 streams the weight side (packed int4 tiles, scales, zero
+        // points) and never waits for the kernel that produced x; warp 3
+        // streams the activation side (int8 tiles, activation scales) after
+        // the programmatic dependency resolves.  Both post their own byte
+        // counts on the shared stage / slot barriers.
+        const bool wside = warp == 0;
         if (elect_one()) {
-            tma_prefetch_desc(&p.tm_w);
-            tma_prefetch_desc(&p.tm_a);
-            tma_prefetch_desc(&p.tm_ws);
-            tma_prefetch_desc(&p.tm_as);
-            if (C::ASYM) tma_prefetch_desc(&p.tm_wz);
-            const uint64_t pol_w = policy_evict_first();
-            const uint64_t pol_a = policy_evict_last();
-            int last_par[8], slot_par[8];
-            for (int i = 0; i < 8; ++i) last_par[i] = -1;
+            if (wside) {
+                tma_prefetch_desc(&p.tm_w);
+                tma_prefetch_desc(&p.tm_ws);
+                if (C::ASYM) tma_prefetch_desc(&p.tm_wz);
+            } else {
+                tma_prefetch_desc(&p.tm_a);
+                tma_prefetch_desc(&p.tm_as);
+                pdl_wait();
+            }
+            const uint64_t pol = wside ? policy_evict_first() : policy_evict_last();
+            const uint32_t stage_tx = wside ? static_cast<uint32_t>(kWStageBytes) : static_cast<uint32_t>(C::A_STAGE);
+            const uint32_t slot_tx = wside ? static_cast<uint32_t>(C::GPK * 128) * ws_elt + (C::ASYM ? C::GPK * 128 * 2 : 0)
+                                           : static_cast<uint32_t>(C::GPK * C::TT * 4);
+            int last_par[12], slot_par[8];
+            for (int i = 0; i < 12; ++i) last_par[i] = -1;
             for (int i = 0; i < 8; ++i) slot_par[i] = -1;
-            bool ok = true;
-
-            // Walk state: (u, kbi) -> stage / slot indices.
-            int u = u0, kbi = 0, stage = 0, slot = 0;
+            int stage = 0, slot = 0;
             uint32_t sph = 0, slph = 0;
-            // --- phase 1: weight-side loads, before the producer of x has finished (PDL) ---
-            int pre = 0, pre_units = 0;
-            {
-                int uu = u0, kk = 0;
-                while (uu < u1 && pre < C::S) {
-                    const Unit un = unit_of(p, uu);
-                    int kb0, kb1;
-                    unit_kblocks<C>(p, un.ut, kb0, kb1);
-                    if (kk == 0) {
-                        if (pre_units >= C::DS) break;
-                        const int sl = pre_units;
-                        mbar_arrive_expect_tx(&bars->sfull[sl], slot_tx);
-                        tma_load_2d(slot_ws(sl), &p.tm_ws, &bars->sfull[sl], un.wt * 128, un.ut * C::GPK);
-                        if (C::ASYM)
-                            tma_load_2d(slot_wz(sl), &p.tm_wz, &bars->sfull[sl], un.wt * 128, un.ut * C::GPK);
-                        slot_par[sl] = 0;
-                        ++pre_units;
-                    }
-                    const int kbg = kb0 + kk;
-                    mbar_arrive_expect_tx(&bars->full[pre], C::STAGE);
-                    tma_load_2d_hint(w_stage(pre), &p.tm_w, &bars->full[pre], kbg * 128, un.wt * 128, pol_w);
-                    last_par[pre] = 0;
-                    ++pre;
-                    if (++kk >= kb1 - kb0) { ++uu; kk = 0; }
-                }
-            }
-            pdl_wait();
-            // --- phase 2: the activation-side loads of the pre-issued stages ---
-            {
-                int uu = u0, kk = 0, n = 0, nu = 0;
-                while (n < pre) {
-                    const Unit un = unit_of(p, uu);
-                    int kb0, kb1;
-                    unit_kblocks<C>(p, un.ut, kb0, kb1);
-                    if (kk == 0) {
-                        tma_load_2d_hint(slot_as(nu), &p.tm_as, &bars->sfull[nu], un.tt * C::TT,
-                                         un.ut * C::GPK, pol_a);
-                        ++nu;
-                    }
-                    const int kbg = kb0 + kk;
-                    tma_load_2d_hint(a_stage(n), &p.tm_a, &bars->full[n], kbg * 256, un.tt * C::TT, pol_a);
-                    tma_load_2d_hint(a_stage(n) + C::TT * 128, &p.tm_a, &bars->full[n], kbg * 256 + 128,
-                                     un.tt * C::TT, pol_a);
-                    ++n;
-                    if (++kk >= kb1 - kb0) { ++uu; kk = 0; }
-                }
-                u = uu;
-                kbi = kk;
-                stage = pre % C::S;
-                sph = (pre / C::S) & 1;
-                slot = pre_units % C::DS;
-                slph = (pre_units / C::DS) & 1;
-            }
-            // --- steady state ---
-            while (ok && u < u1) {
+            bool ok = true;
+            for (int u = u0; ok && u < u1; ++u) {
                 const Unit un = unit_of(p, u);
                 int kb0, kb1;
                 unit_kblocks<C>(p, un.ut, kb0, kb1);
-                if (kbi == 0) {
-                    if (!mbar_wait(&bars->sempty[slot], slph ^ 1, abort_flag, p.status, kWProdSlot)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&bars->sfull[slot], slot_tx);
+                if (!mbar_wait(&bars->sempty[slot], slph ^ 1, abort_flag, p.status, kWProdSlot)) { ok = false; break; }
+                mbar_arrive_expect_tx(&bars->sfull[slot], slot_tx);
+                if (wside) {
                     tma_load_2d(slot_ws(slot), &p.tm_ws, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
                     if (C::ASYM)
                         tma_load_2d(slot_wz(slot), &p.tm_wz, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
-                    tma_load_2d_hint(slot_as(slot), &p.tm_as, &bars->sfull[slot], un.tt * C::TT,
-                                     un.ut * C::GPK, pol_a);
-                    slot_par[slot] = static_cast<int>(slph);
-                    if (++slot == C::DS) { slot = 0; slph ^= 1; }
+                } else {
+                    tma_load_2d_hint(slot_as(slot), &p.tm_as, &bars->sfull[slot], un.tt * C::TT, un.ut * C::GPK, pol);
                 }
-                if (!mbar_wait(&bars->empty[stage], sph ^ 1, abort_flag, p.status, kWProdEmpty)) { ok = false; break; }
-                const int kbg = kb0 + kbi;
-                mbar_arrive_expect_tx(&bars->full[stage], C::STAGE);
-                tma_load_2d_hint(w_stage(stage), &p.tm_w, &bars->full[stage], kbg * 128, un.wt * 128, pol_w);
-                tma_load_2d_hint(a_stage(stage), &p.tm_a, &bars->full[stage], kbg * 256, un.tt * C::TT, pol_a);
-                tma_load_2d_hint(a_stage(stage) + C::TT * 128, &p.tm_a, &bars->full[stage], kbg * 256 + 128,
-                                 un.tt * C::TT, pol_a);
-                last_par[stage] = static_cast<int>(sph);
-                if (++stage == C::S) { stage = 0; sph ^= 1; }
-                if (++kbi >= kb1 - kb0) { ++u; kbi = 0; }
+                slot_par[slot] = static_cast<int>(slph);
+                if (++slot == C::DS) { slot = 0; slph ^= 1; }
+                for (int kbg = kb0; kbg < kb1; ++kbg) {
+                    if (!mbar_wait(&bars->empty[stage], sph ^ 1, abort_flag, p.status, kWProdEmpty)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&bars->full[stage], stage_tx);
+                    if (wside) {
+                        tma_load_2d_hint(w_stage(stage), &p.tm_w, &bars->full[stage], kbg * 128, un.wt * 128, pol);
+                    } else {
+                        tma_load_2d_hint(a_stage(stage), &p.tm_a, &bars->full[stage], kbg * 256, un.tt * C::TT, pol);
+                        tma_load_2d_hint(a_stage(stage) + C::TT * 128, &p.tm_a, &bars->full[stage], kbg * 256 + 128,
+                                         un.tt * C::TT, pol);
+                    }
+                    last_par[stage] = static_cast<int>(sph);
+                    if (++stage == C::S) { stage = 0; sph ^= 1; }
+                }
             }
             // Never leave with a copy in flight: wait (bounded) for the last load of every buffer.
             for (int i = 0; i < C::S; ++i)
@@ -632,6 +625,10 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         uint64_t acc2[C::NC / 2];
 #pragma unroll
         for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
+        Pending pend[2];
+        pend[0].valid = pend[1].valid = 0;
+        pend[0].old = pend[1].old = -1;
+        int npend = 0;
         int slot = 0, sl = 0;
         uint32_t slph = 0, aph = 0;
         bool ok = true;
@@ -694,11 +691,15 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
 
             // ---- end of this CTA's share of tile t: store or hand over ----
             if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
-                if (!out_partials) flush_tile<C>(p, un, u0, u1, cta, nctas, row, col0, ew, lane, nthr, acc2, bars);
+                if (!out_partials) {
+                    flush_tile<C>(p, un, u0, u1, cta, nctas, row, col0, ew, lane, nthr, acc2, pend[npend]);
+                    if (pend[npend].valid && npend < 1) ++npend;
+                }
 #pragma unroll
                 for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
             }
         }
+        if (!out_partials) finish_pending<C>(p, nctas, row, col0, ew, lane, nthr, pend, bars);
     }
 
     // ---------------------------------------------------------------- teardown
