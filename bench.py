@@ -173,26 +173,37 @@ def build_weights(torch, dev, seed=0):
     for i, shape in enumerate(SHAPES):
         K, N = QWQ_SHAPES[shape]
         codes, scale, _ = weight_torch(N, K, GK, seed + i, dev)
-        W[shape] = (ops.pack_int4_grouped(codes, GK), scale.contiguous(), K, N)
+        packed = ops.pack_int4_grouped(codes, GK)
         del codes
+        scale = scale.contiguous()
+        # prepared once at load, like process_weights_after_loading; the raw
+        # layout stays resident for the raw-layout comparison line
+        W[shape] = (packed, scale, K, N, ops.prepare_weights(packed, scale, None, K, GK))
     return W
 
 
+def l2_flush(torch, flush):
+    """Evict L2 by READING a buffer twice its size (a write would leave dirty
+    lines that the next kernel pays to write back)."""
+    return flush.view(torch.int64).sum()
+
+
 def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=3):
-    """GEMM-only launches, L2 flushed before each, CUDA events on the launch stream."""
+    """GEMM-only launches on prepared weights, L2 flushed before each, CUDA
+    events on the launch stream."""
     out = []
     st = torch.cuda.current_stream()
     for (shape, M) in cfgs:
-        packed, scale, K, N = W[shape]
+        packed, scale, K, N, pw = W[shape]
         x = xs[(shape, M)]
         ts = []
         for _ in range(reps):
             ops.linear_quant(x, N, GK)
-            flush.zero_()
+            l2_flush(torch, flush)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(st)
-            ops.linear_gemm(M, K, packed, scale, None, GK, ys[(shape, M)])
+            ops.linear_gemm_prepared(M, pw, ys[(shape, M)])
             e1.record(st)
             e1.synchronize()
             ts.append(e0.elapsed_time(e1) * 1e-3)
@@ -239,35 +250,46 @@ def run_gpu(args, rank, world, local_rank):
 
     def step():
         for (s, M) in cfgs:
-            packed, scale, K, N = W[s]
+            ops.linear_prepared(xs[(s, M)], W[s][4], out=ys[(s, M)])
+
+    def step_raw():
+        for (s, M) in cfgs:
+            packed, scale, K, N, _ = W[s]
             ops.linear(xs[(s, M)], packed, scale, None, GK, out=ys[(s, M)])
 
+    def timed_graph(fn, steps, warmup):
+        fn()                                   # allocates the workspace
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(max(3, warmup)):
+            g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t = e0.elapsed_time(e1) * 1e-3 / steps
+        if world > 1:
+            tt = torch.tensor([t], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        del g
+        return t
+
     sampler.start()
-    step()                                     # allocates the workspace
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        step()
-    for _ in range(max(3, args.warmup)):
-        g.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        g.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    t_step = e0.elapsed_time(e1) * 1e-3 / args.steps
-    if world > 1:
-        t = torch.tensor([t_step], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_step = float(t.item())
+    t_step = timed_graph(step, args.steps, args.warmup)
     value = world * step_bytes / t_step / 1e9
+    t_raw = timed_graph(step_raw, max(3, min(args.steps, 50)), 3)
+    raw_value = world * step_bytes / t_raw / 1e9
     status = ops.workspace_status(dev)
 
     # ---- end to end through the public op, host buffers ----
@@ -279,9 +301,8 @@ def run_gpu(args, rank, world, local_rank):
 
     def e2e_step():
         for (s, M) in cfgs:
-            packed, scale, K, N = W[s]
             xd[(s, M)].copy_(xh[(s, M)], non_blocking=True)
-            y = ops.linear(xd[(s, M)], packed, scale, None, GK)
+            y = ops.linear_prepared(xd[(s, M)], W[s][4])
             yh[(s, M)].copy_(y, non_blocking=True)
 
     n_e2e = max(3, min(args.steps, 20))
@@ -305,7 +326,7 @@ def run_gpu(args, rank, world, local_rank):
            "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * t_e2e, "steps": n_e2e}
 
     # ---- dominant kernel alone (GEMM), cold L2, events per launch ----
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.ones(512 << 20, dtype=torch.uint8, device=dev)
     kt = time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush)
     k_bytes = sum(alg_bytes(M, N, K) for (_, M, K, N, _) in kt)
     k_time = sum(t for *_, t in kt)
@@ -324,7 +345,7 @@ def run_gpu(args, rank, world, local_rank):
     big = {}
     for M in PREFILL_MS:
         for s in SHAPES:
-            packed, scale, K, N = W[s]
+            K, N = W[s][2], W[s][3]
             x = syn.activation_torch(M, K, 200 + M, dev)
             y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             big[(s, M)] = (x, y)
@@ -364,9 +385,12 @@ def run_gpu(args, rank, world, local_rank):
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
-                     "kernel": "w4a8_gemm_kernel (GEMM alone, L2 flushed before each launch)",
+                     "kernel": "w4a8_gemm_kernel (GEMM alone on prepared weights, L2 flushed by a "
+                               "512 MB read before each launch)",
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src},
         "e2e": e2e,
+        "raw_layout": {"value": raw_value, "unit": "GB/s", "ms_per_step": 1e3 * t_raw,
+                       "note": "same sweep on the reference row-major weight layout (2-D tensor copies)"},
         "gpu_launches": launches,
         "clocks": clocks,
         "prefill": {"metric": "W4A8 GEMM int8 TOP/s (prefill)", "value": pre_tops, "unit": "TOP/s",
@@ -394,10 +418,11 @@ def profile_case(spec: str):
     dev = torch.device("cuda", 0)
     codes, scale, _ = syn.weight_torch(N, K, GK, 1, dev)
     packed = ops.pack_int4_grouped(codes, GK)
+    pw = ops.prepare_weights(packed, scale, None, K, GK)
     x = syn.activation_torch(M, K, 2, dev)
     y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     for _ in range(8):
-        ops.linear(x, packed, scale, None, GK, out=y)
+        ops.linear_prepared(x, pw, out=y)
     torch.cuda.synchronize()
     assert ops.workspace_status(dev) == 0
     print(f"profile case {shape} M={M} K={K} N={N}: ok")

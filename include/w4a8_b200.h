@@ -80,6 +80,27 @@ W4A8_API int w4a8_linear_gemm(int64_t M, int64_t K, int64_t N, int32_t group_siz
                      const void* w_scale, int32_t w_scale_dtype, const void* w_zero, void* y,
                      int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- prepared weights: the fast path for weights that are used many times ----
+ * One-time regrouping of the reference layout (packed int4 [N, Kpad/2], scales
+ * and zero points [G, N]) into contiguous, pre-swizzled 16 KB tiles plus
+ * per-row-tile scale rows, so each pipeline stage is filled by one bulk copy.
+ * Plays the part of MidGroupW4A8LinearMethod.process_weights_after_loading
+ * (npu_ops/python/midgroup_quant.py:148-161), which also re-lays scales once
+ * after loading.  `prepared` must be 256-byte aligned. */
+W4A8_API size_t w4a8_prepared_weights_size(int64_t N, int64_t K, int32_t group_size, int32_t w_scale_dtype,
+                                           int32_t has_zero);
+W4A8_API int w4a8_prepare_weights(const void* w_packed, const void* w_scale, int32_t w_scale_dtype,
+                                  const void* w_zero, int64_t N, int64_t K, int32_t group_size, void* prepared,
+                                  size_t prepared_bytes, void* stream);
+/* w4a8_linear on prepared weights (same workspace rules). */
+W4A8_API int w4a8_linear_prepared(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t group_size,
+                                  const void* prepared, int32_t w_scale_dtype, int32_t has_zero, void* y,
+                                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+/* The GEMM half of w4a8_linear_prepared (after w4a8_linear_quant on the same workspace). */
+W4A8_API int w4a8_linear_gemm_prepared(int64_t M, int64_t K, int64_t N, int32_t group_size, const void* prepared,
+                                       int32_t w_scale_dtype, int32_t has_zero, void* y, int64_t ldy,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- activation quantiser (fakequant_lab/quant.py:89-141 semantics) ----
  *   a_q       int8 [M, K] natural order
  *   a_scale   [G, M] bf16 bits or f32 (scale_dtype)

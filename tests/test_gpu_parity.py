@@ -177,6 +177,46 @@ def test_linear_tolerance(orc, M, N, K, gk, asym, sd):
     assert ops.workspace_status() == 0
 
 
+@pytest.mark.parametrize("M,N,K,gk,asym,sd", LINEAR_CASES)
+def test_linear_prepared_matches_raw(orc, M, N, K, gk, asym, sd):
+    """Prepared (tile-order) weights give the same bits as the reference layout."""
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    xb = syn.activation_np(M, K, 5000 + M + K)
+    w = syn.weight_np(N, K, gk, 6000 + N + K, asym=asym, scale_bf16=(sd == "bf16"))
+    packed, ws, wz = _weights(w, gk, dev, torch.bfloat16 if sd == "bf16" else torch.float32)
+    x = _bf16_cuda(xb)
+    pw = ops.prepare_weights(packed, ws, wz, K, gk)
+    y_raw = _bits(ops.linear(x, packed, ws, wz, gk))
+    y_pre = _bits(ops.linear_prepared(x, pw))
+    assert np.array_equal(y_raw, y_pre)
+    y64, _ = orc.linear(xb, w.codes, w.scale, w.zero, gk, exact=True)
+    _close(orc.bf16_to_f32(y_pre), y64)
+    assert ops.workspace_status() == 0
+
+
+def test_linear_prepared_split_and_leading_dims(orc):
+    """linear_quant + linear_gemm_prepared equals linear_prepared; 3-D input."""
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    M, N, K, gk = 12, 640, 5120, 128
+    xb = syn.activation_np(M, K, 41)
+    w = syn.weight_np(N, K, gk, 42)
+    packed, ws, _ = _weights(w, gk, dev)
+    pw = ops.prepare_weights(packed, ws, None, K, gk)
+    x = _bf16_cuda(xb)
+    y1 = ops.linear_prepared(x.view(3, 4, K), pw)
+    assert y1.shape == (3, 4, N)
+    y2 = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    ops.linear_quant(x, N, gk)
+    ops.linear_gemm_prepared(M, pw, y2)
+    assert np.array_equal(_bits(y1.view(M, N)), _bits(y2))
+    with pytest.raises(RuntimeError):
+        ops.linear_prepared(x[:, :1024].contiguous(), pw)          # K mismatch
+
+
 def test_linear_golden(golden, orc):
     """Against FakeQuantLinear._kernel_gemm output stored by make_golden.py."""
     from w4a8_b200 import ops

@@ -90,7 +90,7 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_
 // Per-call geometry and the workspace carve-up.
 struct Plan {
     int64_t M, N, K, Kpad, G;
-    int gk, tt, n_wt, n_tt, upt, units, grid, kb_total, as_ld;
+    int gk, tt, n_wt, n_tt, upt, units, grid, kb_total;
     size_t off_counters, off_as, off_aq, off_part, total;
 };
 
@@ -110,15 +110,14 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
     p.upt = gk <= 256 ? p.kb_total : static_cast<int>(p.G);
     p.units = p.n_wt * p.n_tt * p.upt;
     p.grid = std::max(1, std::min(sms, p.units));
-    p.as_ld = static_cast<int>(round_up(M, 4));
     size_t off = 256;                                                     // status word block
     p.off_counters = off;
     off += round_up(static_cast<int64_t>(p.n_wt) * p.n_tt * 4, 256);
     off = round_up(off, 1024);
-    p.off_as = off;
-    off += round_up(p.G * p.as_ld * 4, 1024);
-    p.off_aq = off;
-    off += round_up(M * p.Kpad, 1024);
+    p.off_as = off;                                                       // [n_tt][G][tt] fp32
+    off += round_up(static_cast<int64_t>(p.n_tt) * p.G * p.tt * 4, 1024);
+    p.off_aq = off;                                                       // [n_tt][kb_total][tt*256]
+    off += round_up(static_cast<int64_t>(p.n_tt) * p.kb_total * p.tt * 256, 1024);
     p.off_part = off;
     off += static_cast<size_t>(2) * p.grid * p.tt * 128 * 4;
     p.total = round_up(off, 1024);
@@ -147,31 +146,31 @@ int run_quant_kernel_layout(const Plan& pl, const void* x, int64_t ldx, uint8_t*
     q.Kpad = static_cast<int>(pl.Kpad);
     q.G = static_cast<int>(pl.G);
     q.gk = pl.gk;
-    q.rows = static_cast<int>(pl.M);
+    q.rows = pl.n_tt * pl.tt;
     q.vec_ok = aligned(x, 16) && (pl.K % 8 == 0) && (ldx % 8 == 0);
     q.aq = reinterpret_cast<int8_t*>(ws + pl.off_aq);
     q.as = reinterpret_cast<float*>(ws + pl.off_as);
-    q.as_ld = pl.as_ld;
+    q.tt = pl.tt;
+    q.kb_total = pl.kb_total;
     const cudaError_t e = launch_quant_act(q, kOutKernel, st, true);
     return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
 }
 
-// Encoded descriptors of one (weights, workspace, shape) combination.  Encoding
-// five tensor maps costs microseconds of host time per call, so recently used
-// sets are kept (a serving loop calls the same few layers over and over).
+// Encoded descriptors of one raw weight set.  Encoding tensor maps costs
+// microseconds of host time per call, so recently used sets are kept (a
+// serving loop calls the same few layers over and over).
 struct MapKey {
     const void* w_packed;
     const void* w_scale;
     const void* w_zero;
-    const void* ws;
-    int64_t M, N, K;
-    int gk, ws_dtype, partials, dev;
+    int64_t N, K;
+    int gk, ws_dtype, dev;
     bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
 };
 
 struct MapEntry {
     MapKey key;
-    CUtensorMap maps[5];
+    CUtensorMap maps[3];
     uint64_t stamp;
     bool used;
 };
@@ -182,82 +181,84 @@ uint64_t g_map_clock = 0;
 std::mutex g_map_mutex;
 
 bool encode_maps(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
-                 bool partials, uint8_t* ws, CUtensorMap* m)
+                 CUtensorMap* m)
 {
     const int gpk = pl.gk <= 256 ? 256 / pl.gk : 1;
     return encode_2d(&m[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, w_packed, pl.Kpad / 2, pl.N, pl.Kpad / 2, 128, 128,
                      CU_TENSOR_MAP_SWIZZLE_128B) &&
-           encode_2d(&m[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, ws + pl.off_aq, pl.Kpad, pl.M, pl.Kpad, 128, pl.tt,
-                     CU_TENSOR_MAP_SWIZZLE_128B) &&
-           (partials
-                // scales are not read in this mode: describe a small region the workspace owns
-                ? encode_2d(&m[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.as_ld, pl.G, pl.as_ld * 4,
-                            128, gpk, CU_TENSOR_MAP_SWIZZLE_NONE)
-                : encode_2d(&m[2],
-                            ws_dtype == W4A8_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                            w_scale, pl.N, pl.G, pl.N * (ws_dtype == W4A8_DTYPE_F32 ? 4 : 2), 128, gpk,
-                            CU_TENSOR_MAP_SWIZZLE_NONE)) &&
-           (w_zero == nullptr ||
-            encode_2d(&m[3], CU_TENSOR_MAP_DATA_TYPE_UINT16, w_zero, pl.N, pl.G, pl.N * 2, 128, gpk,
+           (w_scale == nullptr ||   // the partials mode reads no scales
+            encode_2d(&m[1],
+                      ws_dtype == W4A8_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                      w_scale, pl.N, pl.G, pl.N * (ws_dtype == W4A8_DTYPE_F32 ? 4 : 2), 128, gpk,
                       CU_TENSOR_MAP_SWIZZLE_NONE)) &&
-           encode_2d(&m[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws + pl.off_as, pl.M, pl.G, pl.as_ld * 4, pl.tt, gpk,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
+           (w_zero == nullptr ||
+            encode_2d(&m[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, w_zero, pl.N, pl.G, pl.N * 2, 128, gpk,
+                      CU_TENSOR_MAP_SWIZZLE_NONE));
 }
 
 bool cached_maps(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
-                 bool partials, uint8_t* ws, GemmParams& g)
+                 GemmParams& g)
 {
     MapKey k;
     std::memset(&k, 0, sizeof(k));
     k.w_packed = w_packed;
     k.w_scale = w_scale;
     k.w_zero = w_zero;
-    k.ws = ws;
-    k.M = pl.M;
+    k.ws_dtype = ws_dtype;
     k.N = pl.N;
     k.K = pl.K;
     k.gk = pl.gk;
-    k.ws_dtype = ws_dtype;
-    k.partials = partials ? 1 : 0;
     cudaGetDevice(&k.dev);
     std::lock_guard<std::mutex> lock(g_map_mutex);
     int victim = 0;
-    for (int i = 0; i < kMapCache; ++i) {
-        if (g_maps[i].used && g_maps[i].key == k) {
-            g_maps[i].stamp = ++g_map_clock;
-            std::memcpy(&g.tm_w, &g_maps[i].maps[0], sizeof(CUtensorMap));
-            std::memcpy(&g.tm_a, &g_maps[i].maps[1], sizeof(CUtensorMap));
-            std::memcpy(&g.tm_ws, &g_maps[i].maps[2], sizeof(CUtensorMap));
-            std::memcpy(&g.tm_wz, &g_maps[i].maps[3], sizeof(CUtensorMap));
-            std::memcpy(&g.tm_as, &g_maps[i].maps[4], sizeof(CUtensorMap));
-            return true;
-        }
-        if (g_maps[victim].used && (!g_maps[i].used || g_maps[i].stamp < g_maps[victim].stamp)) victim = i;
+    MapEntry* hit = nullptr;
+    for (int i = 0; i < kMapCache && !hit; ++i) {
+        if (g_maps[i].used && g_maps[i].key == k) hit = &g_maps[i];
+        else if (g_maps[victim].used && (!g_maps[i].used || g_maps[i].stamp < g_maps[victim].stamp)) victim = i;
     }
-    MapEntry& e = g_maps[victim];
-    std::memset(e.maps, 0, sizeof(e.maps));
-    if (!encode_maps(pl, w_packed, w_scale, ws_dtype, w_zero, partials, ws, e.maps)) {
+    if (!hit) {
+        MapEntry& e = g_maps[victim];
+        std::memset(e.maps, 0, sizeof(e.maps));
         e.used = false;
-        return false;
+        if (!encode_maps(pl, w_packed, w_scale, ws_dtype, w_zero, e.maps)) return false;
+        e.key = k;
+        e.used = true;
+        hit = &e;
     }
-    e.key = k;
-    e.used = true;
-    e.stamp = ++g_map_clock;
-    std::memcpy(&g.tm_w, &e.maps[0], sizeof(CUtensorMap));
-    std::memcpy(&g.tm_a, &e.maps[1], sizeof(CUtensorMap));
-    std::memcpy(&g.tm_ws, &e.maps[2], sizeof(CUtensorMap));
-    std::memcpy(&g.tm_wz, &e.maps[3], sizeof(CUtensorMap));
-    std::memcpy(&g.tm_as, &e.maps[4], sizeof(CUtensorMap));
+    hit->stamp = ++g_map_clock;
+    std::memcpy(&g.tm_w, &hit->maps[0], sizeof(CUtensorMap));
+    std::memcpy(&g.tm_ws, &hit->maps[1], sizeof(CUtensorMap));
+    std::memcpy(&g.tm_wz, &hit->maps[2], sizeof(CUtensorMap));
     return true;
 }
 
-int run_gemm(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
-             void* out, int64_t ldy, bool partials, uint8_t* ws, cudaStream_t st)
+// The weight operand of a call: the reference row-major layout, or a buffer
+// made by w4a8_prepare_weights.
+struct Weights {
+    const void* w_packed;   // raw
+    const void* w_scale;    // raw
+    const void* w_zero;     // raw, or null
+    const uint8_t* prepared;
+    bool has_zero;          // prepared: zero points present
+    int32_t ws_dtype;
+};
+
+int run_gemm(const Plan& pl, const Weights& w, void* out, int64_t ldy, bool partials, uint8_t* ws, cudaStream_t st)
 {
-    if (get_encoder() != W4A8_OK) return fail_cuda(cudaErrorNotSupported);
     GemmParams g;
     std::memset(&g, 0, sizeof(g));
-    if (!cached_maps(pl, w_packed, w_scale, ws_dtype, w_zero, partials, ws, g)) return W4A8_ERR_INVALID;
+    const bool asym = w.prepared ? w.has_zero : (w.w_zero != nullptr);
+    if (w.prepared) {
+        const PreparedLayout L = prepared_layout(pl.N, pl.G, pl.kb_total, w.ws_dtype == W4A8_DTYPE_F32 ? 4 : 2, asym);
+        g.w_tiles = w.prepared + L.off_tiles;
+        g.ws_tiles = w.prepared + L.off_ws;
+        g.wz_tiles = asym ? w.prepared + L.off_wz : nullptr;
+    } else {
+        if (get_encoder() != W4A8_OK) return fail_cuda(cudaErrorNotSupported);
+        if (!cached_maps(pl, w.w_packed, w.w_scale, w.ws_dtype, w.w_zero, g)) return W4A8_ERR_INVALID;
+    }
+    g.a_tiles = ws + pl.off_aq;
+    g.as_tiles = reinterpret_cast<const float*>(ws + pl.off_as);
     g.out = out;
     g.partials = reinterpret_cast<float*>(ws + pl.off_part);
     g.counters = reinterpret_cast<int*>(ws + pl.off_counters);
@@ -275,8 +276,8 @@ int run_gemm(const Plan& pl, const void* w_packed, const void* w_scale, int32_t 
     GemmConfig c{};
     c.tt = pl.tt;
     c.gk = pl.gk;
-    c.asym = w_zero != nullptr;
-    c.ws_bf16 = ws_dtype != W4A8_DTYPE_F32;
+    c.asym = asym;
+    c.ws_bf16 = w.ws_dtype != W4A8_DTYPE_F32;
     c.partials = partials;
     const cudaError_t e = launch_gemm(g, c, pl.grid, st, true);
     return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
@@ -344,8 +345,8 @@ int w4a8_linear_gemm(int64_t M, int64_t K, int64_t N, int32_t gk, const void* w_
     if ((rc = device_info(&sms)) != W4A8_OK) return rc;
     const Plan pl = make_plan(M, N, K, gk, sms);
     if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
-    return run_gemm(pl, w_packed, w_scale, ws_dtype, w_zero, y, ldy, false, static_cast<uint8_t*>(workspace),
-                    static_cast<cudaStream_t>(stream));
+    const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
+    return run_gemm(pl, w, y, ldy, false, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 int w4a8_linear(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk, const void* w_packed,
@@ -365,7 +366,8 @@ int w4a8_linear(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
-    return run_gemm(pl, w_packed, w_scale, ws_dtype, w_zero, y, ldy, false, ws, st);
+    const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
+    return run_gemm(pl, w, y, ldy, false, ws, st);
 }
 
 int w4a8_group_partials(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
@@ -384,7 +386,8 @@ int w4a8_group_partials(const void* x, int64_t M, int64_t K, int64_t ldx, int64_
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
-    return run_gemm(pl, w_packed, ws + pl.off_as, W4A8_DTYPE_F32, w_zero, partials, N, true, ws, st);
+    const Weights w{w_packed, nullptr, w_zero, nullptr, false, W4A8_DTYPE_F32};
+    return run_gemm(pl, w, partials, N, true, ws, st);
 }
 
 int w4a8_quant_act(const void* x, int64_t M, int64_t K, int64_t ldx, int32_t gk, int8_t* a_q, void* a_scale,
@@ -472,12 +475,85 @@ int w4a8_midgroup_w4a8_gemm(const int8_t* a_hi, const int8_t* a_lo, const void* 
     m.Kpad = static_cast<int>(pl.Kpad);
     m.G = static_cast<int>(pl.G);
     m.gk = gk;
+    m.rows = pl.n_tt * pl.tt;
     m.aq = reinterpret_cast<int8_t*>(ws + pl.off_aq);
     m.as = reinterpret_cast<float*>(ws + pl.off_as);
-    m.as_ld = pl.as_ld;
+    m.tt = pl.tt;
+    m.kb_total = pl.kb_total;
     cudaError_t e = launch_msd_to_kernel(m, st, true);
     if (e != cudaSuccess) return fail_cuda(e);
-    return run_gemm(pl, w_q, w_scale, W4A8_DTYPE_BF16, w_zero, y, N, false, ws, st);
+    const Weights w{w_q, w_scale, w_zero, nullptr, false, W4A8_DTYPE_BF16};
+    return run_gemm(pl, w, y, N, false, ws, st);
+}
+
+size_t w4a8_prepared_weights_size(int64_t N, int64_t K, int32_t gk, int32_t ws_dtype, int32_t has_zero)
+{
+    if (N <= 0 || K <= 0 || !group_ok(gk) || N % 8 != 0) return 0;
+    if (ws_dtype != W4A8_DTYPE_BF16 && ws_dtype != W4A8_DTYPE_F32) return 0;
+    const int64_t Kpad = kpad_of(K, gk);
+    return static_cast<size_t>(prepared_layout(N, cdiv(K, gk), static_cast<int>(cdiv(Kpad, 256)),
+                                               ws_dtype == W4A8_DTYPE_F32 ? 4 : 2, has_zero != 0).total);
+}
+
+int w4a8_prepare_weights(const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero, int64_t N,
+                         int64_t K, int32_t gk, void* out, size_t out_bytes, void* stream)
+{
+    int rc = check_common(1, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if ((rc = check_weights(w_packed, w_scale, ws_dtype, w_zero)) != W4A8_OK) return rc;
+    const size_t need = w4a8_prepared_weights_size(N, K, gk, ws_dtype, w_zero != nullptr);
+    if (!out || !aligned(out, 256) || out_bytes < need) return W4A8_ERR_INVALID;
+    PrepareParams p{};
+    p.w_packed = static_cast<const uint8_t*>(w_packed);
+    p.w_scale = static_cast<const uint8_t*>(w_scale);
+    p.w_zero = static_cast<const uint16_t*>(w_zero);
+    p.out = static_cast<uint8_t*>(out);
+    p.N = static_cast<int>(N);
+    p.Kpad = static_cast<int>(kpad_of(K, gk));
+    p.G = static_cast<int>(cdiv(K, gk));
+    p.kb_total = static_cast<int>(cdiv(p.Kpad, 256));
+    p.ws_elt = ws_dtype == W4A8_DTYPE_F32 ? 4 : 2;
+    const cudaError_t e = launch_prepare_weights(p, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
+}
+
+int w4a8_linear_prepared(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk, const void* prepared,
+                         int32_t ws_dtype, int32_t has_zero, void* y, int64_t ldy, void* workspace,
+                         size_t workspace_bytes, void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < K || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if (!prepared || !aligned(prepared, 256)) return W4A8_ERR_INVALID;
+    if (ws_dtype != W4A8_DTYPE_BF16 && ws_dtype != W4A8_DTYPE_F32) return W4A8_ERR_UNSUPPORTED;
+    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
+    const Weights w{nullptr, nullptr, nullptr, static_cast<const uint8_t*>(prepared), has_zero != 0, ws_dtype};
+    return run_gemm(pl, w, y, ldy, false, ws, st);
+}
+
+int w4a8_linear_gemm_prepared(int64_t M, int64_t K, int64_t N, int32_t gk, const void* prepared, int32_t ws_dtype,
+                              int32_t has_zero, void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                              void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!prepared || !aligned(prepared, 256) || !y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
+    if (ws_dtype != W4A8_DTYPE_BF16 && ws_dtype != W4A8_DTYPE_F32) return W4A8_ERR_UNSUPPORTED;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    const Weights w{nullptr, nullptr, nullptr, static_cast<const uint8_t*>(prepared), has_zero != 0, ws_dtype};
+    return run_gemm(pl, w, y, ldy, false, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 int w4a8_workspace_status(void* workspace, int32_t reset, void* stream)

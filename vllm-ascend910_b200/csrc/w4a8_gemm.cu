@@ -38,15 +38,16 @@ namespace w4a8 {
 
 namespace {
 
-constexpr int kWStageBytes = 128 * 128;   // 128 weight rows x 128 B (256 int4)
+constexpr int kWTileBytes = 128 * 128;    // 128 weight rows x 128 B (256 int4)
 constexpr int kNumPreWarps = 8;           // weight producer, 2 MMA issuers, activation producer, 4 converters
 constexpr int kActProducerWarp = 3;
 constexpr int kNumIssuers = 2;            // one thread issues a tcgen05.mma every ~80 cycles: use two
 constexpr int kSmemBudget = 227 * 1024 - 1024;
+constexpr int kBarBytes = 1024;
 
 // wait-site ids for the status word
-enum { kWProdEmpty = 1, kWProdSlot, kWConvFull, kWConvAEmpty, kWConvSlot, kWMmaFull, kWMmaAFull,
-       kWMmaAccEmpty, kWEpiSlot, kWEpiAccFull, kWDrain };
+enum { kWProdEmpty = 1, kWActEmpty, kWProdSlot, kWConvFull, kWConvAEmpty, kWMmaFull, kWMmaAFull, kWMmaAccEmpty,
+       kWEpiSlot, kWEpiAccFull, kWDrain };
 
 template <int TT_, int GK_, bool ASYM_>
 struct Cfg {
@@ -73,37 +74,51 @@ struct Cfg {
     static constexpr int BCH = TOTCH < 2 ? TOTCH : 2;        // chunks per tcgen05.ld batch
     static constexpr int NACC_FIT = ACC_COLS / (CG * TT);
     static constexpr int NACC = NACC_FIT > 8 ? 8 : NACC_FIT;           // accumulator slots
-    static constexpr int A_STAGE = TT * 256;
-    static constexpr int STAGE = kWStageBytes + A_STAGE;
     __host__ __device__ static constexpr int r128(int x) { return (x + 127) / 128 * 128; }
-    static constexpr int SL_WS = GPK * 128 * 4;              // sized for fp32 scales
-    static constexpr int SL_WZ = ASYM ? GPK * 128 * 2 : 0;
+    // Shared memory, in this order (tiles first: they need 1024-byte alignment):
+    //   S_W weight tiles     16 KB each, released by the converters
+    //   S_A activation tiles TT x 256 B each, released by the MMA
+    //   S_W zero-point rows  (asymmetric) the unit's GPK x 128 bf16, loaded with its first tile
+    //   DS scale slots       one unit's [GPK][128] weight scales (sized for fp32) and
+    //                        [GPK][TT] activation scales, filled by the activation
+    //                        producer, released by the epilogue
+    //   barriers
+    static constexpr int A_STAGE = TT * 256;
+    static constexpr int WZ_BYTES = ASYM ? GPK * 128 * 2 : 0;
+    static constexpr int WZ_SLOT = r128(WZ_BYTES);
+    static constexpr int SL_WS = GPK * 128 * 4;
     static constexpr int SL_AS = GPK * TT * 4;
-    static constexpr int SLOT = r128(SL_WS) + r128(SL_WZ) + r128(SL_AS);
-    static constexpr int DS = TT <= 64 ? 8 : 4;              // scale slots
-    static constexpr int S_FIT = (kSmemBudget - DS * SLOT - 2048) / STAGE;
-    static constexpr int S = S_FIT > 12 ? 12 : S_FIT;        // pipeline stages
-    static constexpr int BAR_OFF = S * STAGE + DS * SLOT;
-    static constexpr int SMEM = BAR_OFF + 1024 + 1024;       // + barriers + alignment slack
+    static constexpr int SLOT = r128(SL_WS) + r128(SL_AS);
+    static constexpr int DS = TT <= 32 ? 12 : 8;
+    static constexpr int S_A = TT <= 16 ? 8 : (TT <= 32 ? 6 : (TT <= 64 ? 4 : 3));
+    static constexpr int S_W_FIT = (kSmemBudget - kBarBytes - DS * SLOT - S_A * A_STAGE) / (kWTileBytes + WZ_SLOT);
+    static constexpr int S_W = S_W_FIT > 16 ? 16 : S_W_FIT;
+    static constexpr int OFF_A = S_W * kWTileBytes;
+    static constexpr int OFF_WZ = OFF_A + S_A * A_STAGE;
+    static constexpr int OFF_SL = OFF_WZ + S_W * WZ_SLOT;
+    static constexpr int BAR_OFF = OFF_SL + DS * SLOT;
+    static constexpr int SMEM = BAR_OFF + kBarBytes + 1024;  // + alignment slack
     static constexpr int TMEM_COLS = 512;
-    static_assert(S >= 3, "pipeline too shallow");
+    static_assert(S_W >= 3 && S_A >= 2, "pipeline too shallow");
     static_assert(NACC >= 2, "need at least two accumulator slots");
     static_assert(NC % 16 == 0, "epilogue works in 16-column chunks");
+    static_assert(OFF_A % 1024 == 0 && OFF_WZ % 1024 == 0, "tile alignment");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct Bars {
-    uint64_t full[12], empty[12];
-    uint64_t sfull[8], sempty[8];
-    uint64_t afull[4], aempty[4];
-    uint64_t accfull[8], accempty[8];
+    uint64_t wfull[16], wempty[16];     // weight tiles
+    uint64_t afull[8], aempty[8];       // activation tiles
+    uint64_t tfull[4], tempty[4];       // converted weights in TMEM
+    uint64_t accfull[8], accempty[8];   // accumulator slots
+    uint64_t sfull[12], sempty[12];     // scale slots
     uint64_t drain[2];
     uint32_t tmem_base;
     int abort;
     int last_flag;
 };
 
-static_assert(sizeof(Bars) <= 1024, "barrier block overflows its reservation");
-static_assert(Cfg<16, 128, false>::S <= 12, "stage barriers");
+static_assert(sizeof(Bars) <= kBarBytes, "barrier block overflows its reservation");
 
 struct Unit {
     int t, wt, tt, ut;
@@ -126,6 +141,19 @@ __device__ __forceinline__ Unit unit_of(const GemmParams& p, int u)
     r.wt = r.t / p.n_tt;
     r.tt = r.t - r.wt * p.n_tt;
     return r;
+}
+
+// The unit after `r` (units run K-unit fastest, then token tile, then weight tile).
+__device__ __forceinline__ void unit_next(const GemmParams& p, Unit& r)
+{
+    if (++r.ut == p.units_per_tile) {
+        r.ut = 0;
+        ++r.t;
+        if (++r.tt == p.n_tt) {
+            r.tt = 0;
+            ++r.wt;
+        }
+    }
 }
 
 template <class C>
@@ -347,29 +375,33 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     int u0, u1;
     cta_range(p, cta, nctas, u0, u1);
 
-    auto w_stage = [&](int s) { return smem + s * C::STAGE; };
-    auto a_stage = [&](int s) { return smem + s * C::STAGE + kWStageBytes; };
-    auto slot_ws = [&](int s) { return smem + C::S * C::STAGE + s * C::SLOT; };
-    auto slot_wz = [&](int s) { return slot_ws(s) + C::r128(C::SL_WS); };
-    auto slot_as = [&](int s) { return reinterpret_cast<float*>(slot_wz(s) + C::r128(C::SL_WZ)); };
+    auto w_tile = [&](int s) { return smem + s * kWTileBytes; };
+    auto a_stage = [&](int s) { return smem + C::OFF_A + s * C::A_STAGE; };
+    auto w_zero = [&](int s) { return smem + C::OFF_WZ + s * C::WZ_SLOT; };
+    auto slot_ws = [&](int s) { return smem + C::OFF_SL + s * C::SLOT; };
+    auto slot_as = [&](int s) { return reinterpret_cast<float*>(slot_ws(s) + C::r128(C::SL_WS)); };
 
     // ---------------------------------------------------------------- setup
     if (threadIdx.x == 0) {
-        for (int i = 0; i < C::S; ++i) {
-            mbar_init(&bars->full[i], 2);               // weight and activation producers
-            mbar_init(&bars->empty[i], 4 + kNumIssuers);  // 4 converter warps + each issuer's commit
+        for (int i = 0; i < C::S_W; ++i) {
+            mbar_init(&bars->wfull[i], 1);                  // weight producer (+ bytes)
+            mbar_init(&bars->wempty[i], 4);                 // 4 converter warps
         }
-        for (int i = 0; i < C::DS; ++i) {
-            mbar_init(&bars->sfull[i], 2);
-            mbar_init(&bars->sempty[i], 4 + 4 * C::E);  // converter + epilogue warps
+        for (int i = 0; i < C::S_A; ++i) {
+            mbar_init(&bars->afull[i], 1);                  // activation producer (+ bytes)
+            mbar_init(&bars->aempty[i], kNumIssuers);       // each issuer's commit
         }
         for (int i = 0; i < C::NA; ++i) {
-            mbar_init(&bars->afull[i], 4);
-            mbar_init(&bars->aempty[i], kNumIssuers);
+            mbar_init(&bars->tfull[i], 4);
+            mbar_init(&bars->tempty[i], kNumIssuers);
         }
         for (int i = 0; i < C::NACC; ++i) {
             mbar_init(&bars->accfull[i], 1);
             mbar_init(&bars->accempty[i], 4 * C::E);
+        }
+        for (int i = 0; i < C::DS; ++i) {
+            mbar_init(&bars->sfull[i], 1);                  // activation producer (+ bytes)
+            mbar_init(&bars->sempty[i], 4 * C::E);          // epilogue warps
         }
         mbar_init(&bars->drain[0], 1);
         mbar_init(&bars->drain[1], 1);
@@ -386,93 +418,115 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     const uint32_t tbase = bars->tmem_base;
     volatile int* abort_flag = &bars->abort;
     pdl_launch_dependents();
-
     const uint32_t ws_elt = ws_bf16 ? 2u : 4u;
 
     if (warp == 0 || warp == kActProducerWarp) {
         // ============================================================ producers
-        // Warp 0 streams the weight side (packed int4 tiles, scales, zero
-        // points) and never waits for the kernel that produced x; warp 3
-        // streams the activation side (int8 tiles, activation scales) after
-        // the programmatic dependency resolves.  Both post their own byte
-        // counts on the shared stage / slot barriers.
+        // Warp 0 streams weight tiles (and, asymmetric, the unit's zero points
+        // with its first tile); it never waits for the epilogue nor for the
+        // kernel that produced x.  Warp 3, after the programmatic dependency
+        // resolves, streams activation tiles and fills each unit's scale slot
+        // (weight and activation scales) for the epilogue.  Each copy is one
+        // instruction.
         const bool wside = warp == 0;
+        const bool prepared = p.w_tiles != nullptr;
         if (elect_one()) {
-            if (wside) {
+            if (wside && !prepared) {
                 tma_prefetch_desc(&p.tm_w);
-                tma_prefetch_desc(&p.tm_ws);
                 if (C::ASYM) tma_prefetch_desc(&p.tm_wz);
-            } else {
-                tma_prefetch_desc(&p.tm_a);
-                tma_prefetch_desc(&p.tm_as);
-                pdl_wait();
             }
+            if (!wside && !prepared && !out_partials) tma_prefetch_desc(&p.tm_ws);
+            if (!wside) pdl_wait();
             const uint64_t pol = wside ? policy_evict_first() : policy_evict_last();
-            const uint32_t stage_tx = wside ? static_cast<uint32_t>(kWStageBytes) : static_cast<uint32_t>(C::A_STAGE);
-            const uint32_t slot_tx = wside ? static_cast<uint32_t>(C::GPK * 128) * ws_elt + (C::ASYM ? C::GPK * 128 * 2 : 0)
-                                           : static_cast<uint32_t>(C::GPK * C::TT * 4);
-            int last_par[12], slot_par[8];
-            for (int i = 0; i < 12; ++i) last_par[i] = -1;
-            for (int i = 0; i < 8; ++i) slot_par[i] = -1;
-            int stage = 0, slot = 0;
-            uint32_t sph = 0, slph = 0;
+            const int ns = wside ? C::S_W : C::S_A;
+            uint64_t* fullb = wside ? bars->wfull : bars->afull;
+            uint64_t* emptyb = wside ? bars->wempty : bars->aempty;
+            int stage = 0, issued = 0, slot = 0, sissued = 0;
+            uint32_t ph = 0, slph = 0;
             bool ok = true;
-            for (int u = u0; ok && u < u1; ++u) {
-                const Unit un = unit_of(p, u);
-                int kb0, kb1;
+            Unit un = unit_of(p, u0);
+            for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
+                int kb0, kb1, g0, g1;
                 unit_kblocks<C>(p, un.ut, kb0, kb1);
-                if (!mbar_wait(&bars->sempty[slot], slph ^ 1, abort_flag, p.status, kWProdSlot)) { ok = false; break; }
-                mbar_arrive_expect_tx(&bars->sfull[slot], slot_tx);
-                if (wside) {
-                    tma_load_2d(slot_ws(slot), &p.tm_ws, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
-                    if (C::ASYM)
-                        tma_load_2d(slot_wz(slot), &p.tm_wz, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
-                } else {
-                    tma_load_2d_hint(slot_as(slot), &p.tm_as, &bars->sfull[slot], un.tt * C::TT, un.ut * C::GPK, pol);
-                }
-                slot_par[slot] = static_cast<int>(slph);
-                if (++slot == C::DS) { slot = 0; slph ^= 1; }
-                for (int kbg = kb0; kbg < kb1; ++kbg) {
-                    if (!mbar_wait(&bars->empty[stage], sph ^ 1, abort_flag, p.status, kWProdEmpty)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&bars->full[stage], stage_tx);
-                    if (wside) {
-                        tma_load_2d_hint(w_stage(stage), &p.tm_w, &bars->full[stage], kbg * 128, un.wt * 128, pol);
+                unit_groups<C>(p, un.ut, g0, g1);
+                if (!wside) {
+                    if (!mbar_wait(&bars->sempty[slot], slph ^ 1, abort_flag, p.status, kWProdSlot)) break;
+                    if (out_partials) {
+                        mbar_arrive(&bars->sfull[slot]);      // the partials mode reads no scales
                     } else {
-                        tma_load_2d_hint(a_stage(stage), &p.tm_a, &bars->full[stage], kbg * 256, un.tt * C::TT, pol);
-                        tma_load_2d_hint(a_stage(stage) + C::TT * 128, &p.tm_a, &bars->full[stage], kbg * 256 + 128,
-                                         un.tt * C::TT, pol);
+                        const uint32_t ng = static_cast<uint32_t>(g1 - g0);
+                        const uint32_t wsb = prepared ? ng * 128u * ws_elt : C::GPK * 128u * ws_elt;
+                        const uint32_t asb = ng * static_cast<uint32_t>(C::TT * 4);
+                        mbar_arrive_expect_tx(&bars->sfull[slot], wsb + asb);
+                        if (prepared)
+                            bulk_load(slot_ws(slot), p.ws_tiles + (static_cast<int64_t>(un.wt) * p.G + g0) * 128 * ws_elt,
+                                      wsb, &bars->sfull[slot], pol);
+                        else
+                            tma_load_2d(slot_ws(slot), &p.tm_ws, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
+                        bulk_load(slot_as(slot), p.as_tiles + (static_cast<int64_t>(un.tt) * p.G + g0) * C::TT, asb,
+                                  &bars->sfull[slot], pol);
                     }
-                    last_par[stage] = static_cast<int>(sph);
-                    if (++stage == C::S) { stage = 0; sph ^= 1; }
+                    ++sissued;
+                    if (++slot == C::DS) { slot = 0; slph ^= 1; }
+                }
+                for (int kbg = kb0; kbg < kb1; ++kbg) {
+                    if (!mbar_wait(&emptyb[stage], ph ^ 1, abort_flag, p.status, wside ? kWProdEmpty : kWActEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    if (wside) {
+                        const bool zp = C::ASYM && kbg == kb0;
+                        const uint32_t zb = zp ? (prepared ? static_cast<uint32_t>(g1 - g0) * 256u : C::GPK * 256u) : 0u;
+                        mbar_arrive_expect_tx(&fullb[stage], kWTileBytes + zb);
+                        if (prepared)
+                            bulk_load(w_tile(stage), p.w_tiles + (static_cast<int64_t>(un.wt) * p.kb_total + kbg) * kWTileBytes,
+                                      kWTileBytes, &fullb[stage], pol);
+                        else
+                            tma_load_2d_hint(w_tile(stage), &p.tm_w, &fullb[stage], kbg * 128, un.wt * 128, pol);
+                        if (zp) {
+                            if (prepared)
+                                bulk_load(w_zero(stage), p.wz_tiles + (static_cast<int64_t>(un.wt) * p.G + g0) * 256, zb,
+                                          &fullb[stage], pol);
+                            else
+                                tma_load_2d(w_zero(stage), &p.tm_wz, &fullb[stage], un.wt * 128, un.ut * C::GPK);
+                        }
+                    } else {
+                        mbar_arrive_expect_tx(&fullb[stage], static_cast<uint32_t>(C::A_STAGE));
+                        bulk_load(a_stage(stage), p.a_tiles + (static_cast<int64_t>(un.tt) * p.kb_total + kbg) * C::A_STAGE,
+                                  C::A_STAGE, &fullb[stage], pol);
+                    }
+                    ++issued;
+                    if (++stage == ns) { stage = 0; ph ^= 1; }
                 }
             }
-            // Never leave with a copy in flight: wait (bounded) for the last load of every buffer.
-            for (int i = 0; i < C::S; ++i)
-                if (last_par[i] >= 0) mbar_wait(&bars->full[i], static_cast<uint32_t>(last_par[i]), abort_flag, p.status, kWDrain);
-            for (int i = 0; i < C::DS; ++i)
-                if (slot_par[i] >= 0) mbar_wait(&bars->sfull[i], static_cast<uint32_t>(slot_par[i]), abort_flag, p.status, kWDrain);
+            // Never leave with a copy in flight: wait (bounded) for the last
+            // copy into each stage (copy i went to stage i % ns, phase i / ns).
+            for (int i = issued > ns ? issued - ns : 0; i < issued; ++i)
+                mbar_wait(&fullb[i % ns], static_cast<uint32_t>((i / ns) & 1), abort_flag, p.status, kWDrain);
+            for (int i = sissued > C::DS ? sissued - C::DS : 0; i < sissued; ++i)
+                mbar_wait(&bars->sfull[i % C::DS], static_cast<uint32_t>((i / C::DS) & 1), abort_flag, p.status, kWDrain);
         }
     } else if (warp <= kNumIssuers) {
         // ============================================================ MMA issuers
         // Both issuers walk every k-block; issuer i issues the MMAs of the
         // accumulator slots whose global index is i mod 2, and both commit the
-        // k-block's A buffer and stage back (each covering its own MMAs).
+        // k-block's TMEM A buffer and activation tile back (each covering its own MMAs).
         const int me = warp - 1;
         if (elect_one()) {
             const uint32_t idesc = idesc_i8(128, TT);
-            int stage = 0, ab = 0, sl = 0, gsl = 0;
-            uint32_t sph = 0, abph = 0, slph = 0;
+            int sa = 0, ab = 0, sl = 0, gsl = 0;
+            uint32_t saph = 0, abph = 0, slph = 0;
             bool ok = true;
-            for (int u = u0; ok && u < u1; ++u) {
-                const Unit un = unit_of(p, u);
+            Unit un = unit_of(p, u0);
+            for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
                 int kb0, kb1, g0, g1;
                 unit_kblocks<C>(p, un.ut, kb0, kb1);
                 unit_groups<C>(p, un.ut, g0, g1);
                 for (int kbg = kb0; kbg < kb1; ++kbg) {
-                    if (!mbar_wait(&bars->full[stage], sph, abort_flag, p.status, kWMmaFull)) { ok = false; break; }
-                    if (!mbar_wait(&bars->afull[ab], abph, abort_flag, p.status, kWMmaAFull)) { ok = false; break; }
+                    if (!mbar_wait(&bars->afull[sa], saph, abort_flag, p.status, kWMmaFull)) { ok = false; break; }
+                    if (!mbar_wait(&bars->tfull[ab], abph, abort_flag, p.status, kWMmaAFull)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_smem = smem_u32(a_stage(stage));
+                    const uint32_t a_smem = smem_u32(a_stage(sa));
                     const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * 64);
                     if (C::GK <= 256) {
                         for (int g = g0; g < g1; ++g) {
@@ -520,10 +574,10 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                             if (++sl == C::NACC) { sl = 0; slph ^= 1; }
                         }
                     }
-                    tc_commit(&bars->aempty[ab]);
-                    tc_commit(&bars->empty[stage]);
+                    tc_commit(&bars->tempty[ab]);
+                    tc_commit(&bars->aempty[sa]);
                     if (++ab == C::NA) { ab = 0; abph ^= 1; }
-                    if (++stage == C::S) { stage = 0; sph ^= 1; }
+                    if (++sa == C::S_A) { sa = 0; saph ^= 1; }
                 }
             }
             // Wait for every MMA issued by this thread before TMEM can be released.
@@ -532,33 +586,34 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         }
     } else if (warp < kNumPreWarps) {
         // ============================================================ converters
+        // Unpack one weight tile per k-block into a TMEM A buffer and hand the
+        // shared-memory tile straight back to the producer.
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        int stage = 0, ab = 0, slot = 0;
-        uint32_t sph = 0, abph = 0, slph = 0;
+        int stage = 0, ab = 0;
+        uint32_t sph = 0, abph = 0;
         bool ok = true;
-        for (int u = u0; ok && u < u1; ++u) {
-            const Unit un = unit_of(p, u);
+        uint32_t bias[C::GPK];
+#pragma unroll
+        for (int i = 0; i < C::GPK; ++i) bias[i] = 0x78787878u;   // zero point 0
+        Unit un = unit_of(p, u0);
+        for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
             int kb0, kb1;
             unit_kblocks<C>(p, un.ut, kb0, kb1);
-            uint32_t bias[C::GPK];
-#pragma unroll
-            for (int i = 0; i < C::GPK; ++i) bias[i] = 0x78787878u;   // zero point 0
-            if (C::ASYM) {
-                if (!warp_wait(&bars->sfull[slot], slph, abort_flag, p.status, kWConvSlot)) { ok = false; break; }
-                const uint16_t* wz = reinterpret_cast<const uint16_t*>(slot_wz(slot));
-#pragma unroll
-                for (int i = 0; i < C::GPK; ++i) {
-                    const int zu = static_cast<int>(bf16_bits_to_f32(wz[i * 128 + row])) + 8;
-                    bias[i] = static_cast<uint32_t>((0x80 - zu) & 0xFF) * 0x01010101u;
-                }
-            }
             for (int kbg = kb0; kbg < kb1; ++kbg) {
-                if (!warp_wait(&bars->full[stage], sph, abort_flag, p.status, kWConvFull)) { ok = false; break; }
-                if (!warp_wait(&bars->aempty[ab], abph ^ 1, abort_flag, p.status, kWConvAEmpty)) { ok = false; break; }
+                if (!warp_wait(&bars->wfull[stage], sph, abort_flag, p.status, kWConvFull)) { ok = false; break; }
+                if (C::ASYM && kbg == kb0) {
+                    const uint16_t* wz = reinterpret_cast<const uint16_t*>(w_zero(stage));
+#pragma unroll
+                    for (int i = 0; i < C::GPK; ++i) {
+                        const int zu = static_cast<int>(bf16_bits_to_f32(wz[i * 128 + row])) + 8;
+                        bias[i] = static_cast<uint32_t>((0x80 - zu) & 0xFF) * 0x01010101u;
+                    }
+                }
+                if (!warp_wait(&bars->tempty[ab], abph ^ 1, abort_flag, p.status, kWConvAEmpty)) { ok = false; break; }
                 tc_fence_after();
-                const uint8_t* wrow = w_stage(stage) + row * 128;
+                const uint8_t* wrow = w_tile(stage) + row * 128;
                 const uint32_t a_tmem = tbase + lane_off + static_cast<uint32_t>(ab * 64);
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
@@ -584,17 +639,13 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&bars->afull[ab]);
-                    mbar_arrive(&bars->empty[stage]);
+                    mbar_arrive(&bars->tfull[ab]);
+                    mbar_arrive(&bars->wempty[stage]);
                 }
                 __syncwarp();
                 if (++ab == C::NA) { ab = 0; abph ^= 1; }
-                if (++stage == C::S) { stage = 0; sph ^= 1; }
+                if (++stage == C::S_W) { stage = 0; sph ^= 1; }
             }
-            if (!ok) break;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->sempty[slot]);
-            if (++slot == C::DS) { slot = 0; slph ^= 1; }
         }
     } else {
         // ============================================================ epilogue
@@ -629,11 +680,11 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         pend[0].valid = pend[1].valid = 0;
         pend[0].old = pend[1].old = -1;
         int npend = 0;
-        int slot = 0, sl = 0;
-        uint32_t slph = 0, aph = 0;
+        int sl = 0, slot = 0;
+        uint32_t aph = 0, slph = 0;
         bool ok = true;
-        for (int u = u0; ok && u < u1; ++u) {
-            const Unit un = unit_of(p, u);
+        Unit un = unit_of(p, u0);
+        for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
             int g0, g1;
             unit_groups<C>(p, un.ut, g0, g1);
             if (!warp_wait(&bars->sfull[slot], slph, abort_flag, p.status, kWEpiSlot)) { ok = false; break; }
@@ -665,7 +716,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         const int c = b0 + q, gi = c / NCH, i = c % NCH;
                         const int g = gs + gi;
                         if (g >= g1) continue;
-                        const int gl = g - g0;           // group index within the unit's scale slot
+                        const int gl = g - g0;           // group index within the unit's scale entry
                         if (!out_partials) {
                             float wsv = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gl * 128 + row])
                                                 : reinterpret_cast<const float*>(wsb)[gl * 128 + row];
@@ -708,6 +759,51 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, C::TMEM_COLS);
+    }
+}
+
+// Regroup raw weights into the prepared layout (one thread per 16-byte chunk
+// of a tile, then per scale / zero element); rows past N and bytes past Kpad
+// are written as zero.
+__global__ void prepare_weights_kernel(const PrepareParams p)
+{
+    const int n_wt = (p.N + 127) / 128;
+    const int64_t chunks = static_cast<int64_t>(n_wt) * p.kb_total * 128 * 8;
+    const int64_t scal = static_cast<int64_t>(n_wt) * p.G * 128;
+    const int rowb = p.Kpad / 2;
+    const PreparedLayout L = prepared_layout(p.N, p.G, p.kb_total, p.ws_elt, p.w_zero != nullptr);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks + scal;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        if (i < chunks) {
+            const int c = static_cast<int>(i & 7);
+            const int r = static_cast<int>((i >> 3) & 127);
+            const int64_t tile = i >> 10;                      // wt * kb_total + kb
+            const int kb = static_cast<int>(tile % p.kb_total);
+            const int wt = static_cast<int>(tile / p.kb_total);
+            const int n = wt * 128 + r;
+            const int byte = kb * 128 + c * 16;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (n < p.N && byte < rowb)
+                v = *reinterpret_cast<const uint4*>(p.w_packed + static_cast<int64_t>(n) * rowb + byte);
+            *reinterpret_cast<uint4*>(p.out + L.off_tiles + tile * 16384 + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+        } else {
+            const int64_t j = i - chunks;                      // (wt * G + g) * 128 + r
+            const int r = static_cast<int>(j & 127);
+            const int64_t wg = j >> 7;
+            const int g = static_cast<int>(wg % p.G);
+            const int wt = static_cast<int>(wg / p.G);
+            const int n = wt * 128 + r;
+            const bool in = n < p.N;
+            if (p.ws_elt == 4)
+                reinterpret_cast<float*>(p.out + L.off_ws)[j] =
+                    in ? reinterpret_cast<const float*>(p.w_scale)[static_cast<int64_t>(g) * p.N + n] : 0.0f;
+            else
+                reinterpret_cast<uint16_t*>(p.out + L.off_ws)[j] =
+                    in ? reinterpret_cast<const uint16_t*>(p.w_scale)[static_cast<int64_t>(g) * p.N + n] : 0;
+            if (p.w_zero)
+                reinterpret_cast<uint16_t*>(p.out + L.off_wz)[j] =
+                    in ? p.w_zero[static_cast<int64_t>(g) * p.N + n] : 0;
+        }
     }
 }
 
@@ -781,6 +877,12 @@ cudaError_t launch_gemm(const GemmParams& p, const GemmConfig& c, int grid, cuda
         case 128: return launch_tt<128>(p, c, grid, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_prepare_weights(const PrepareParams& p, cudaStream_t stream)
+{
+    prepare_weights_kernel<<<148 * 8, 256, 0, stream>>>(p);
+    return cudaGetLastError();
 }
 
 size_t gemm_smem_bytes(const GemmConfig& c)

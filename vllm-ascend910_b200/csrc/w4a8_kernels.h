@@ -16,10 +16,10 @@ struct QuantParams {
     int M, K, Kpad, G, gk;
     int rows;            // rows to emit: M, or Mp for the MSD form
     int vec_ok;          // 16-byte vector loads are legal for this x
-    // kOutKernel
-    int8_t* aq;          // [M, Kpad] operand order
-    float* as;           // [G, as_ld]
-    int as_ld;
+    // kOutKernel: the GEMM's activation tiles (see gemm_act_tile_offset)
+    int8_t* aq;          // [n_tt][kb_total][TT * 256] bytes, 128-byte swizzled
+    float* as;           // [n_tt][G][TT]
+    int tt, kb_total;
     // kOutPublic
     int8_t* q;           // [M, K]
     void* scale;         // [G, M] bf16 bits or fp32
@@ -38,18 +38,38 @@ struct MsdToKernelParams {
     const uint16_t* a_scale; // [G, scale_ld] bf16 bits
     int scale_ld;
     int M, Kpad, G, gk;
-    int8_t* aq;              // [M, Kpad]
-    float* as;               // [G, as_ld]
-    int as_ld;
+    int rows;                // n_tt * tt: rows of the tile layout (>= M)
+    int8_t* aq;              // activation tiles, as in QuantParams
+    float* as;
+    int tt, kb_total;
 };
+
+// Byte offset of activation code (row, padded position) inside the GEMM's
+// activation tiles: tile (row / tt, pos / 256) holds tt rows x 256 codes as two
+// halves of tt x 128 bytes, each in the 128-byte-swizzled order the MMA's
+// shared-memory descriptor expects (16-byte chunk c of row r stored at chunk
+// c ^ (r % 8)).  One 1-D bulk copy moves a tile.
+__host__ __device__ inline int64_t gemm_act_tile_offset(int row, int pos, int tt, int kb_total)
+{
+    const int r = row % tt, t = row / tt, kb = pos >> 8, w = pos & 255;
+    const int h = w >> 7, c = (w & 127) >> 4, b = w & 15;
+    return (static_cast<int64_t>(t) * kb_total + kb) * (tt * 256) + h * (tt * 128) + r * 128 +
+           ((c ^ (r & 7)) << 4) + b;
+}
 
 // The GEMM's view of one call.  Tensor maps are built on the host.
 struct alignas(64) GemmParams {
+    // raw (reference-layout) weights, read with 2-D tensor copies
     CUtensorMap tm_w;    // packed int4 weights [N, Kpad/2] bytes, box {128 B, 128 rows}, SW128
-    CUtensorMap tm_a;    // int8 activations [M, Kpad] bytes, box {128 B, TT rows}, SW128
     CUtensorMap tm_ws;   // weight scales [G, N] (fp32 or bf16), box {128, GPK}
     CUtensorMap tm_wz;   // weight zero points [G, N] bf16, box {128, GPK} (asymmetric only)
-    CUtensorMap tm_as;   // activation scales [G, M] fp32 (row stride as_ld), box {TT, GPK}
+    // prepared weights (w4a8_prepare_weights), read with 1-D bulk copies; null = raw path
+    const uint8_t* w_tiles;   // [n_wt][kb_total][16384] swizzled packed int4 tiles
+    const uint8_t* ws_tiles;  // [n_wt][G][128] scales (fp32 or bf16)
+    const uint8_t* wz_tiles;  // [n_wt][G][128] bf16 zero points (asymmetric only)
+    // activations from the quantiser, read with 1-D bulk copies
+    const uint8_t* a_tiles;   // [n_tt][kb_total][TT * 256] (gemm_act_tile_offset)
+    const float* as_tiles;    // [n_tt][G][TT]
     void* out;           // y bf16 [M, N] (row stride ldy), or int32 partials [G, M, N]
     float* partials;     // stream-K partial tiles: [2 * grid][TT][128] fp32
     int* counters;       // [n_tiles] arrival counters, zero between calls
@@ -57,6 +77,32 @@ struct alignas(64) GemmParams {
     int M, N, Kpad, G;
     int64_t ldy;
     int n_wt, n_tt, units_per_tile, total_units, kb_total;
+};
+
+// Prepared weight layout: the packed int4 weights regrouped into one
+// contiguous, pre-swizzled 16 KB tile per (128-row tile, 256-element k-block),
+// followed by the scales and zero points regrouped per row tile.
+struct PreparedLayout {
+    int64_t off_tiles, off_ws, off_wz, total;
+};
+
+__host__ __device__ inline PreparedLayout prepared_layout(int64_t N, int64_t G, int kb_total, int ws_elt, bool zero)
+{
+    const int64_t n_wt = (N + 127) / 128;
+    PreparedLayout L;
+    L.off_tiles = 0;
+    L.off_ws = n_wt * kb_total * 16384;
+    L.off_wz = L.off_ws + ((n_wt * G * 128 * ws_elt + 255) / 256) * 256;
+    L.total = L.off_wz + (zero ? ((n_wt * G * 128 * 2 + 255) / 256) * 256 : 0);
+    return L;
+}
+
+struct PrepareParams {
+    const uint8_t* w_packed;   // [N, Kpad/2]
+    const uint8_t* w_scale;    // [G, N]
+    const uint16_t* w_zero;    // [G, N] or null
+    uint8_t* out;
+    int N, Kpad, G, kb_total, ws_elt;
 };
 
 struct GemmConfig {
@@ -68,6 +114,7 @@ struct GemmConfig {
 };
 
 cudaError_t launch_quant_act(const QuantParams& p, int out_kind, cudaStream_t stream, bool pdl);
+cudaError_t launch_prepare_weights(const PrepareParams& p, cudaStream_t stream);
 cudaError_t launch_msd_to_kernel(const MsdToKernelParams& p, cudaStream_t stream, bool pdl);
 
 // Launches the GEMM on `grid` persistent CTAs.  Returns cudaErrorInvalidValue

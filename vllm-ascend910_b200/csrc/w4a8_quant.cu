@@ -16,9 +16,11 @@
 // shuffles (plus a shared-memory step when a group spans several warps).
 //
 // Three output forms, selected at compile time:
-//   kOutKernel  int8 codes in the GEMM's operand order (each 8 positions stored
-//               as k0 k2 k4 k6 k1 k3 k5 k7, matching the nibble order the GEMM
-//               unpacks weights in) + fp32 scales [G, as_ld]
+//   kOutKernel  the GEMM's activation tiles: int8 codes in operand order (each
+//               8 positions stored as k0 k2 k4 k6 k1 k3 k5 k7, matching the
+//               nibble order the GEMM unpacks weights in) inside swizzled
+//               [token tile][k-block] tiles, zero-filled past M and K, plus
+//               fp32 scales [token tile][group][row]
 //   kOutPublic  int8 codes [M, K] natural order + scales [G, M] (bf16 or fp32)
 //               + negated sums [G, M]
 //   kOutMsd     the reference op's four tensors: MSD int4 planes a_hi/a_lo
@@ -78,7 +80,9 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
     const int pos = (blockIdx.x * kQThreads + tid) * 8;   // padded position of element 0
     const int gk = p.gk;
     const int tpg = gk >> 3;                               // threads per group
-    const bool active = pos < p.Kpad;
+    // the GEMM's tiles span whole k-blocks: positions up to kb_total*256 exist there
+    const int span = (kOut == kOutKernel) ? p.kb_total * 256 : p.Kpad;
+    const bool active = pos < span;
     const bool real_row = row < p.M;
     const int g = pos / gk;
 
@@ -86,7 +90,7 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
     float xv[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) xv[i] = 0.0f;
-    if (active && real_row) {
+    if (active && real_row && pos < p.Kpad) {
         const uint16_t* xr = p.x + static_cast<int64_t>(row) * p.ldx;
         if (p.vec_ok && pos + 8 <= p.K) {
             const uint4 v = *reinterpret_cast<const uint4*>(xr + pos);
@@ -142,14 +146,14 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
     const bool leader = (pos % gk) == 0;
 
     if (kOut == kOutKernel) {
-        if (!real_row) return;
-        // operand order: k0 k2 k4 k6 | k1 k3 k5 k7
+        // operand order: k0 k2 k4 k6 | k1 k3 k5 k7 (rows >= M and positions >= K are zero)
         const uint32_t lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) |
                             (static_cast<uint32_t>(q[6] & 0xFF) << 24);
         const uint32_t hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) |
                             (static_cast<uint32_t>(q[7] & 0xFF) << 24);
-        *reinterpret_cast<uint2*>(p.aq + static_cast<int64_t>(row) * p.Kpad + pos) = make_uint2(lo, hi);
-        if (leader) p.as[static_cast<int64_t>(g) * p.as_ld + row] = s;
+        *reinterpret_cast<uint2*>(p.aq + gemm_act_tile_offset(row, pos, p.tt, p.kb_total)) = make_uint2(lo, hi);
+        if (leader && g < p.G)
+            p.as[(static_cast<int64_t>(row / p.tt) * p.G + g) * p.tt + row % p.tt] = real_row ? s : 0.0f;
     } else if (kOut == kOutPublic) {
         if (!real_row) return;
         int8_t* qr = p.q + static_cast<int64_t>(row) * p.K;
@@ -197,31 +201,34 @@ __global__ void __launch_bounds__(kQThreads) msd_to_kernel_kernel(const MsdToKer
     pdl_wait();
     const int row = blockIdx.y;
     const int pos = (blockIdx.x * kQThreads + threadIdx.x) * 8;
+    const bool real_row = row < p.M;
     if (threadIdx.x == 0) {
         const int g0 = (blockIdx.x * kQPos) / p.gk;
         const int g1 = min(p.G, ((blockIdx.x + 1) * kQPos + p.gk - 1) / p.gk);
         for (int g = g0; g < g1; ++g)
-            p.as[static_cast<int64_t>(g) * p.as_ld + row] =
-                bf16_bits_to_f32(p.a_scale[static_cast<int64_t>(g) * p.scale_ld + row]);
+            p.as[(static_cast<int64_t>(row / p.tt) * p.G + g) * p.tt + row % p.tt] =
+                real_row ? bf16_bits_to_f32(p.a_scale[static_cast<int64_t>(g) * p.scale_ld + row]) : 0.0f;
     }
-    if (pos >= p.Kpad) return;
-    const int64_t o = static_cast<int64_t>(row) * (p.Kpad / 2) + pos / 2;
-    const uint32_t hw = *reinterpret_cast<const uint32_t*>(p.a_hi + o);
-    const uint32_t lw = *reinterpret_cast<const uint32_t*>(p.a_lo + o);
-    int q[8];
+    if (pos >= p.kb_total * 256) return;
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (real_row && pos < p.Kpad) {
+        const int64_t o = static_cast<int64_t>(row) * (p.Kpad / 2) + pos / 2;
+        const uint32_t hw = *reinterpret_cast<const uint32_t*>(p.a_hi + o);
+        const uint32_t lw = *reinterpret_cast<const uint32_t*>(p.a_lo + o);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int hn = static_cast<int>((hw >> (4 * i)) & 0xFu);
-        const int ln = static_cast<int>((lw >> (4 * i)) & 0xFu);
-        const int hv = (hn & 8) ? hn - 16 : hn;
-        const int lv = (ln & 8) ? ln - 16 : ln;
-        q[i] = 16 * hv + lv + 8;
+        for (int i = 0; i < 8; ++i) {
+            const int hn = static_cast<int>((hw >> (4 * i)) & 0xFu);
+            const int ln = static_cast<int>((lw >> (4 * i)) & 0xFu);
+            const int hv = (hn & 8) ? hn - 16 : hn;
+            const int lv = (ln & 8) ? ln - 16 : ln;
+            q[i] = 16 * hv + lv + 8;
+        }
     }
     const uint32_t lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) |
                         (static_cast<uint32_t>(q[6] & 0xFF) << 24);
     const uint32_t hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) |
                         (static_cast<uint32_t>(q[7] & 0xFF) << 24);
-    *reinterpret_cast<uint2*>(p.aq + static_cast<int64_t>(row) * p.Kpad + pos) = make_uint2(lo, hi);
+    *reinterpret_cast<uint2*>(p.aq + gemm_act_tile_offset(row, pos, p.tt, p.kb_total)) = make_uint2(lo, hi);
 }
 
 template <typename Kern, typename Params>
@@ -245,7 +252,8 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, const Params& prm, cuda
 
 cudaError_t launch_quant_act(const QuantParams& p, int out_kind, cudaStream_t stream, bool pdl)
 {
-    const dim3 grid((p.Kpad + kQPos - 1) / kQPos, p.rows);
+    const int span = out_kind == kOutKernel ? p.kb_total * 256 : p.Kpad;
+    const dim3 grid((span + kQPos - 1) / kQPos, p.rows);
     const dim3 block(kQThreads);
     switch (out_kind) {
         case kOutKernel: return launch_pdl(quant_act_kernel<kOutKernel>, grid, block, p, stream, pdl);
@@ -256,7 +264,7 @@ cudaError_t launch_quant_act(const QuantParams& p, int out_kind, cudaStream_t st
 
 cudaError_t launch_msd_to_kernel(const MsdToKernelParams& p, cudaStream_t stream, bool pdl)
 {
-    const dim3 grid((p.Kpad + kQPos - 1) / kQPos, p.M);
+    const dim3 grid((p.kb_total * 256 + kQPos - 1) / kQPos, p.rows);
     return launch_pdl(msd_to_kernel_kernel, grid, dim3(kQThreads), p, stream, pdl);
 }
 

@@ -39,6 +39,12 @@ SIGNATURES = [
     ("w4a8_linear_quant", ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i32, _p, _sz, _p]),
     ("w4a8_linear_gemm", ctypes.c_int,
      [_i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _p, _sz, _p]),
+    ("w4a8_prepared_weights_size", _sz, [_i64, _i64, _i32, _i32, _i32]),
+    ("w4a8_prepare_weights", ctypes.c_int, [_p, _p, _i32, _p, _i64, _i64, _i32, _p, _sz, _p]),
+    ("w4a8_linear_prepared", ctypes.c_int,
+     [_p, _i64, _i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),
+    ("w4a8_linear_gemm_prepared", ctypes.c_int,
+     [_i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),
     ("w4a8_quant_act", ctypes.c_int, [_p, _i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p]),
     ("w4a8_midgroup_quant_a", ctypes.c_int, [_p, _i64, _i64, _i32, _i64, _p, _p, _p, _p, _p]),
     ("w4a8_midgroup_gemm_workspace_size", _sz, [_i64, _i64, _i64, _i32]),

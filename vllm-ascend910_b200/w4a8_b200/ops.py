@@ -240,6 +240,72 @@ def linear_gemm(M: int, K: int, w_packed, w_scale, w_zero, group_size: int, y: t
     _lib.check(rc, "w4a8_linear_gemm")
 
 
+class PreparedWeight:
+    """A linear layer's weights regrouped once into the GEMM's tile order
+    (``w4a8_prepare_weights``): the same values as (w_packed, w_scale, w_zero),
+    read by the kernel with one bulk copy per pipeline stage."""
+
+    __slots__ = ("buf", "N", "K", "group_size", "ws_dtype", "has_zero")
+
+    def __init__(self, buf: torch.Tensor, N: int, K: int, group_size: int, ws_dtype: int, has_zero: bool):
+        self.buf, self.N, self.K, self.group_size = buf, N, K, group_size
+        self.ws_dtype, self.has_zero = ws_dtype, has_zero
+
+    def ptr(self) -> int:
+        return (self.buf.data_ptr() + 255) & ~255
+
+
+def prepare_weights(w_packed: torch.Tensor, w_scale: torch.Tensor, w_zero: Optional[torch.Tensor],
+                    K: int, group_size: int) -> PreparedWeight:
+    """Regroup reference-layout weights for the bulk-copy GEMM path (one-time, like
+    ``process_weights_after_loading`` in npu_ops/python/midgroup_quant.py:148-161)."""
+    _check_cuda(w_packed, w_scale, w_zero)
+    N = _check_weight(w_packed, w_scale, w_zero, K, group_size)
+    w_packed, w_scale = w_packed.contiguous(), w_scale.contiguous()
+    w_zero = None if w_zero is None else w_zero.contiguous()
+    sd = _lib.DTYPE_F32 if w_scale.dtype == torch.float32 else _lib.DTYPE_BF16
+    L = _lib.lib()
+    nbytes = L.w4a8_prepared_weights_size(N, K, group_size, sd, 1 if w_zero is not None else 0)
+    _check(nbytes > 0, "prepare_weights: unsupported shape")
+    buf = torch.empty(nbytes + 256, dtype=torch.uint8, device=w_packed.device)
+    pw = PreparedWeight(buf, N, K, group_size, sd, w_zero is not None)
+    rc = L.w4a8_prepare_weights(w_packed.data_ptr(), w_scale.data_ptr(), sd, _ptr(w_zero), N, K, group_size,
+                                pw.ptr(), nbytes, _stream(w_packed.device))
+    _lib.check(rc, "w4a8_prepare_weights")
+    return pw
+
+
+def linear_prepared(x: torch.Tensor, pw: PreparedWeight, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``linear`` on prepared weights (bit-identical results)."""
+    _check(x.dtype == torch.bfloat16, "w4a8 linear: x must be bfloat16")
+    _check_cuda(x, pw.buf)
+    lead, K = x.shape[:-1], x.shape[-1]
+    _check(K == pw.K, f"w4a8 linear: x has K={K}, weights were prepared for K={pw.K}")
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M, N = x2.shape[0], pw.N
+    y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    if M == 0:
+        return y.reshape(*lead, N)
+    L = _lib.lib()
+    ws, wsb = workspace(L.w4a8_linear_workspace_size(M, N, K, pw.group_size), x.device)
+    rc = L.w4a8_linear_prepared(x2.data_ptr(), M, K, x2.stride(0), N, pw.group_size, pw.ptr(), pw.ws_dtype,
+                                1 if pw.has_zero else 0, y.data_ptr(), y.stride(0), ws, wsb, _stream(x.device))
+    _lib.check(rc, "w4a8_linear_prepared")
+    return y.reshape(*lead, N)
+
+
+def linear_gemm_prepared(M: int, pw: PreparedWeight, y: torch.Tensor) -> None:
+    """Second half of ``linear_prepared`` after ``linear_quant(x2, pw.N, pw.group_size)``."""
+    L = _lib.lib()
+    ws, wsb = workspace(L.w4a8_linear_workspace_size(M, pw.N, pw.K, pw.group_size), y.device)
+    rc = L.w4a8_linear_gemm_prepared(M, pw.K, pw.N, pw.group_size, pw.ptr(), pw.ws_dtype,
+                                     1 if pw.has_zero else 0, y.data_ptr(), y.stride(0), ws, wsb,
+                                     _stream(y.device))
+    _lib.check(rc, "w4a8_linear_gemm_prepared")
+
+
 def group_partials(x: torch.Tensor, w_packed: torch.Tensor, w_zero: Optional[torch.Tensor],
                    group_size: int) -> torch.Tensor:
     """int32 P[G, M, N] = sum_{k in g} A_q * (W - wz), from the tensor-core path."""
