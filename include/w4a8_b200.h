@@ -101,6 +101,28 @@ W4A8_API int w4a8_linear_gemm_prepared(int64_t M, int64_t K, int64_t N, int32_t 
                                        int32_t w_scale_dtype, int32_t has_zero, void* y, int64_t ldy,
                                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- w4a8_linear without a caller-provided workspace ----
+ * No counterpart in the reference.  Same arguments, checks and results as
+ * w4a8_linear minus the workspace: its scratch is one fixed
+ * W4A8_FIXED_SCRATCH_BYTES array of device memory per device, declared in the
+ * library itself, so the call allocates nothing.  For callers that cannot
+ * allocate device memory at the call site: foreign-language hosts that hold
+ * no device allocator, and serving loops whose allocator must not be entered
+ * (cudaMalloc synchronises the device; a caching allocator may be in a
+ * no-growth phase).
+ *   - Returns W4A8_ERR_WORKSPACE when the call would need more scratch than
+ *     the array holds (16 MiB covers M <= 64 on 27648 x 7168 weights).
+ *   - The first call on a device looks the array up, clears it and waits for
+ *     the clear on `stream`: make that first call before any stream capture.
+ *   - Every call on a device shares the one array: calls that overlap in time
+ *     (different streams, threads) race on it and must be serialised by the
+ *     caller. */
+#define W4A8_FIXED_SCRATCH_BYTES ((size_t)16 << 20)
+W4A8_API int w4a8_linear_fixed_scratch(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N,
+                                       int32_t group_size, const void* w_packed, const void* w_scale,
+                                       int32_t w_scale_dtype, const void* w_zero, void* y, int64_t ldy,
+                                       void* stream);
+
 /* ---- activation quantiser (fakequant_lab/quant.py:89-141 semantics) ----
  *   a_q       int8 [M, K] natural order
  *   a_scale   [G, M] bf16 bits or f32 (scale_dtype)

@@ -291,6 +291,33 @@ int check_weights(const void* w_packed, const void* w_scale, int32_t ws_dtype, c
     return W4A8_OK;
 }
 
+// ---- fixed scratch for w4a8_linear_fixed_scratch ----
+// One statically sized device array per device context (module data, not an
+// allocation).  Its address is looked up once per device with that device
+// current; the whole array is cleared on that first call, after which the
+// kernels leave the arrival counters and the status word at zero themselves.
+__device__ __align__(256) uint8_t g_fixed_scratch[W4A8_FIXED_SCRATCH_BYTES];
+uint8_t* g_fixed_ptr[kMaxDev];
+std::mutex g_fixed_mutex;
+
+int fixed_scratch(cudaStream_t st, uint8_t** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_cuda(e);
+    if (dev < 0 || dev >= kMaxDev) return W4A8_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(g_fixed_mutex);
+    if (g_fixed_ptr[dev] == nullptr) {
+        void* ptr = nullptr;
+        if ((e = cudaGetSymbolAddress(&ptr, g_fixed_scratch)) != cudaSuccess) return fail_cuda(e);
+        if ((e = cudaMemsetAsync(ptr, 0, W4A8_FIXED_SCRATCH_BYTES, st)) != cudaSuccess) return fail_cuda(e);
+        if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return fail_cuda(e);
+        g_fixed_ptr[dev] = static_cast<uint8_t*>(ptr);
+    }
+    *out = g_fixed_ptr[dev];
+    return W4A8_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -365,6 +392,28 @@ int w4a8_linear(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int
     if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
+    const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
+    return run_gemm(pl, w, y, ldy, false, ws, st);
+}
+
+int w4a8_linear_fixed_scratch(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
+                              const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero, void* y,
+                              int64_t ldy, void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < K || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if ((rc = check_weights(w_packed, w_scale, ws_dtype, w_zero)) != W4A8_OK) return rc;
+    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (pl.total > W4A8_FIXED_SCRATCH_BYTES) return W4A8_ERR_WORKSPACE;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = nullptr;
+    if ((rc = fixed_scratch(st, &ws)) != W4A8_OK) return rc;
     if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
     const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
     return run_gemm(pl, w, y, ldy, false, ws, st);

@@ -20,6 +20,7 @@ ERR_WORKSPACE = -4
 ERR_DEVICE = -5
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
+FIXED_SCRATCH_BYTES = 16 << 20   # W4A8_FIXED_SCRATCH_BYTES
 
 _L = None
 
@@ -45,6 +46,8 @@ SIGNATURES = [
      [_p, _i64, _i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),
     ("w4a8_linear_gemm_prepared", ctypes.c_int,
      [_i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),
+    ("w4a8_linear_fixed_scratch", ctypes.c_int,
+     [_p, _i64, _i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _p]),
     ("w4a8_quant_act", ctypes.c_int, [_p, _i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p]),
     ("w4a8_midgroup_quant_a", ctypes.c_int, [_p, _i64, _i64, _i32, _i64, _p, _p, _p, _p, _p]),
     ("w4a8_midgroup_gemm_workspace_size", _sz, [_i64, _i64, _i64, _i32]),
