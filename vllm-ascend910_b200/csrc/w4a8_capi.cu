@@ -107,7 +107,10 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
     p.n_wt = static_cast<int>(cdiv(N, 128));
     p.n_tt = static_cast<int>(cdiv(M, p.tt));
     p.kb_total = static_cast<int>(cdiv(p.Kpad, 256));
-    p.upt = gk <= 256 ? p.kb_total : static_cast<int>(p.G);
+    // units per tile: stages of two k-blocks for token tiles <= 32 (GK <= 256),
+    // one k-block for larger tiles, one group for GK = 1024 (the kernel's Cfg)
+    const int ks = p.tt <= 32 ? 2 : 1;
+    p.upt = gk <= 256 ? static_cast<int>(cdiv(p.kb_total, ks)) : static_cast<int>(p.G);
     p.units = p.n_wt * p.n_tt * p.upt;
     p.grid = std::max(1, std::min(sms, p.units));
     size_t off = 256;                                                     // status word block
@@ -164,7 +167,7 @@ struct MapKey {
     const void* w_scale;
     const void* w_zero;
     int64_t N, K;
-    int gk, ws_dtype, dev;
+    int gk, ws_dtype, gpu, dev;
     bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
 };
 
@@ -180,10 +183,13 @@ MapEntry g_maps[kMapCache];
 uint64_t g_map_clock = 0;
 std::mutex g_map_mutex;
 
+// Groups per GEMM unit (the scale / zero-point box height): the kernel's Cfg::GPU.
+int groups_per_unit(const Plan& pl) { return pl.gk <= 256 ? (pl.tt <= 32 ? 2 : 1) * (256 / pl.gk) : 1; }
+
 bool encode_maps(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
                  CUtensorMap* m)
 {
-    const int gpk = pl.gk <= 256 ? 256 / pl.gk : 1;
+    const int gpk = groups_per_unit(pl);
     return encode_2d(&m[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, w_packed, pl.Kpad / 2, pl.N, pl.Kpad / 2, 128, 128,
                      CU_TENSOR_MAP_SWIZZLE_128B) &&
            (w_scale == nullptr ||   // the partials mode reads no scales
@@ -205,6 +211,7 @@ bool cached_maps(const Plan& pl, const void* w_packed, const void* w_scale, int3
     k.w_scale = w_scale;
     k.w_zero = w_zero;
     k.ws_dtype = ws_dtype;
+    k.gpu = groups_per_unit(pl);
     k.N = pl.N;
     k.K = pl.K;
     k.gk = pl.gk;

@@ -54,46 +54,53 @@ struct Cfg {
     static constexpr int TT = TT_;
     static constexpr int GK = GK_;
     static constexpr bool ASYM = ASYM_;
-    static constexpr int GPK = GK <= 256 ? 256 / GK : 1;     // groups per unit
-    static constexpr int KPU = GK <= 256 ? 1 : GK / 256;     // k-blocks per unit (max)
+    // Pipeline granularity.  Every hand-over between warps costs a few
+    // hundred cycles of mbarrier latency, so small token tiles move two
+    // k-blocks (32 KB of int4 weights) per stage.
+    static constexpr int KS = TT <= 32 ? 2 : 1;              // k-blocks per stage
+    static constexpr int GPK = GK <= 256 ? 256 / GK : 1;     // groups per k-block
+    static constexpr int UKB = GK <= 256 ? KS : GK / 256;    // k-blocks per unit (max)
+    static constexpr int GPU = GK <= 256 ? KS * GPK : 1;     // groups per unit (max)
     static constexpr bool SYM16 = !ASYM && GK <= 256;
     static constexpr bool MAGIC = GK <= 256;                 // magic-initialised accumulators
     static constexpr int E = TT <= 32 ? 1 : 2;               // epilogue warpgroups
     static constexpr int NC = TT / E;                        // accumulator columns per thread
     static constexpr int NCH = NC / 16;                      // 16-column TMEM chunks per thread
     static constexpr int THREADS = (kNumPreWarps + 4 * E) * 32;
-    // TMEM: NA A buffers of 64 columns (one k-block of int8 weights), the rest
-    // for accumulator slots.
-    static constexpr int NA = TT <= 64 ? 4 : 2;
-    static constexpr int ACC0 = NA * 64;
+    // TMEM: NA A buffers of KS x 64 columns (the stage's int8 weights), the
+    // rest for accumulator slots of CG groups x TT columns.
+    static constexpr int ABUF = KS * 64;
+    static constexpr int NA = (TT <= 64 ? 256 : 128) / ABUF;
+    static constexpr int ACC0 = NA * ABUF;
     static constexpr int ACC_COLS = 512 - ACC0;
-    // groups per accumulator slot: a whole unit when its columns fit one
-    // 32-register load batch of the epilogue and the ring stays >= 4 deep
-    static constexpr int CG = (GPK * NC <= 32 && ACC_COLS / (GPK * TT) >= 4) ? GPK : 1;
+    static constexpr int CG_FIT = ACC_COLS / (4 * TT);       // keeps >= 4 slots
+    static constexpr int CG = GPU <= CG_FIT ? GPU : (CG_FIT >= 4 ? 4 : (CG_FIT >= 2 ? 2 : 1));
     static constexpr int TOTCH = CG * NCH;                   // 16-column chunks per slot and thread
     static constexpr int BCH = TOTCH < 2 ? TOTCH : 2;        // chunks per tcgen05.ld batch
     static constexpr int NACC_FIT = ACC_COLS / (CG * TT);
     static constexpr int NACC = NACC_FIT > 8 ? 8 : NACC_FIT;           // accumulator slots
     __host__ __device__ static constexpr int r128(int x) { return (x + 127) / 128 * 128; }
     // Shared memory, in this order (tiles first: they need 1024-byte alignment):
-    //   S_W weight tiles     16 KB each, released by the converters
-    //   S_A activation tiles TT x 256 B each, released by the MMA
-    //   S_W zero-point rows  (asymmetric) the unit's GPK x 128 bf16, loaded with its first tile
-    //   DS scale slots       one unit's [GPK][128] weight scales (sized for fp32) and
-    //                        [GPK][TT] activation scales, filled by the activation
-    //                        producer, released by the epilogue
+    //   S_W weight stages     KS x 16 KB, released by the converters
+    //   S_A activation stages KS x TT x 256 B, released by the MMA
+    //   S_W zero-point rows   (asymmetric) the unit's GPU x 128 bf16, loaded with its first stage
+    //   DS scale slots        one unit's [GPU][128] weight scales (sized for fp32) and
+    //                         [GPU][TT] activation scales, filled by the activation
+    //                         producer, released by the epilogue
     //   barriers
-    static constexpr int A_STAGE = TT * 256;
-    static constexpr int WZ_BYTES = ASYM ? GPK * 128 * 2 : 0;
+    static constexpr int A_TILE = TT * 256;
+    static constexpr int A_STAGE = KS * A_TILE;
+    static constexpr int W_STAGE = KS * kWTileBytes;
+    static constexpr int WZ_BYTES = ASYM ? GPU * 128 * 2 : 0;
     static constexpr int WZ_SLOT = r128(WZ_BYTES);
-    static constexpr int SL_WS = GPK * 128 * 4;
-    static constexpr int SL_AS = GPK * TT * 4;
+    static constexpr int SL_WS = GPU * 128 * 4;
+    static constexpr int SL_AS = GPU * TT * 4;
     static constexpr int SLOT = r128(SL_WS) + r128(SL_AS);
-    static constexpr int DS = TT <= 32 ? 12 : 8;
-    static constexpr int S_A = TT <= 16 ? 8 : (TT <= 32 ? 6 : (TT <= 64 ? 4 : 3));
-    static constexpr int S_W_FIT = (kSmemBudget - kBarBytes - DS * SLOT - S_A * A_STAGE) / (kWTileBytes + WZ_SLOT);
+    static constexpr int DS = 8;
+    static constexpr int S_A = TT <= 16 ? 4 : (TT <= 32 ? 2 : (TT <= 64 ? 4 : 3));
+    static constexpr int S_W_FIT = (kSmemBudget - kBarBytes - DS * SLOT - S_A * A_STAGE) / (W_STAGE + WZ_SLOT);
     static constexpr int S_W = S_W_FIT > 16 ? 16 : S_W_FIT;
-    static constexpr int OFF_A = S_W * kWTileBytes;
+    static constexpr int OFF_A = S_W * W_STAGE;
     static constexpr int OFF_WZ = OFF_A + S_A * A_STAGE;
     static constexpr int OFF_SL = OFF_WZ + S_W * WZ_SLOT;
     static constexpr int BAR_OFF = OFF_SL + DS * SLOT;
@@ -101,6 +108,7 @@ struct Cfg {
     static constexpr int TMEM_COLS = 512;
     static_assert(S_W >= 3 && S_A >= 2, "pipeline too shallow");
     static_assert(NACC >= 2, "need at least two accumulator slots");
+    static_assert(GPU % CG == 0, "slots split a unit evenly");
     static_assert(NC % 16 == 0, "epilogue works in 16-column chunks");
     static_assert(OFF_A % 1024 == 0 && OFF_WZ % 1024 == 0, "tile alignment");
     static_assert(SMEM <= 227 * 1024, "shared memory");
@@ -111,7 +119,7 @@ struct Bars {
     uint64_t afull[8], aempty[8];       // activation tiles
     uint64_t tfull[4], tempty[4];       // converted weights in TMEM
     uint64_t accfull[8], accempty[8];   // accumulator slots
-    uint64_t sfull[12], sempty[12];     // scale slots
+    uint64_t sfull[8], sempty[8];       // scale slots
     uint64_t drain[2];
     uint32_t tmem_base;
     int abort;
@@ -156,23 +164,20 @@ __device__ __forceinline__ void unit_next(const GemmParams& p, Unit& r)
     }
 }
 
+// A unit (the stream-K work item and the epilogue's step) is UKB k-blocks:
+// one stage of KS k-blocks when GK <= 256, one GK = 1024 group otherwise.
 template <class C>
 __device__ __forceinline__ void unit_kblocks(const GemmParams& p, int ut, int& kb0, int& kb1)
 {
-    if (C::GK <= 256) {
-        kb0 = ut;
-        kb1 = ut + 1;
-    } else {
-        kb0 = ut * C::KPU;
-        kb1 = min(kb0 + C::KPU, p.kb_total);
-    }
+    kb0 = ut * C::UKB;
+    kb1 = min(kb0 + C::UKB, p.kb_total);
 }
 
 template <class C>
 __device__ __forceinline__ void unit_groups(const GemmParams& p, int ut, int& g0, int& g1)
 {
-    g0 = ut * C::GPK;
-    g1 = min(g0 + C::GPK, p.G);
+    g0 = ut * C::GPU;
+    g1 = min(g0 + C::GPU, p.G);
 }
 
 __device__ __forceinline__ void cta_range(const GemmParams& p, int c, int C, int& u0, int& u1)
@@ -375,7 +380,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     int u0, u1;
     cta_range(p, cta, nctas, u0, u1);
 
-    auto w_tile = [&](int s) { return smem + s * kWTileBytes; };
+    auto w_tile = [&](int s) { return smem + s * C::W_STAGE; };
     auto a_stage = [&](int s) { return smem + C::OFF_A + s * C::A_STAGE; };
     auto w_zero = [&](int s) { return smem + C::OFF_WZ + s * C::WZ_SLOT; };
     auto slot_ws = [&](int s) { return smem + C::OFF_SL + s * C::SLOT; };
@@ -455,45 +460,49 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         mbar_arrive(&bars->sfull[slot]);      // the partials mode reads no scales
                     } else {
                         const uint32_t ng = static_cast<uint32_t>(g1 - g0);
-                        const uint32_t wsb = prepared ? ng * 128u * ws_elt : C::GPK * 128u * ws_elt;
+                        const uint32_t wsb = prepared ? ng * 128u * ws_elt : C::GPU * 128u * ws_elt;
                         const uint32_t asb = ng * static_cast<uint32_t>(C::TT * 4);
                         mbar_arrive_expect_tx(&bars->sfull[slot], wsb + asb);
                         if (prepared)
                             bulk_load(slot_ws(slot), p.ws_tiles + (static_cast<int64_t>(un.wt) * p.G + g0) * 128 * ws_elt,
                                       wsb, &bars->sfull[slot], pol);
                         else
-                            tma_load_2d(slot_ws(slot), &p.tm_ws, &bars->sfull[slot], un.wt * 128, un.ut * C::GPK);
+                            tma_load_2d(slot_ws(slot), &p.tm_ws, &bars->sfull[slot], un.wt * 128, g0);
                         bulk_load(slot_as(slot), p.as_tiles + (static_cast<int64_t>(un.tt) * p.G + g0) * C::TT, asb,
                                   &bars->sfull[slot], pol);
                     }
                     ++sissued;
                     if (++slot == C::DS) { slot = 0; slph ^= 1; }
                 }
-                for (int kbg = kb0; kbg < kb1; ++kbg) {
+                for (int kbs = kb0; kbs < kb1; kbs += C::KS) {
+                    const int kn = min(C::KS, kb1 - kbs);       // k-blocks in this stage
                     if (!mbar_wait(&emptyb[stage], ph ^ 1, abort_flag, p.status, wside ? kWProdEmpty : kWActEmpty)) {
                         ok = false;
                         break;
                     }
                     if (wside) {
-                        const bool zp = C::ASYM && kbg == kb0;
-                        const uint32_t zb = zp ? (prepared ? static_cast<uint32_t>(g1 - g0) * 256u : C::GPK * 256u) : 0u;
-                        mbar_arrive_expect_tx(&fullb[stage], kWTileBytes + zb);
-                        if (prepared)
-                            bulk_load(w_tile(stage), p.w_tiles + (static_cast<int64_t>(un.wt) * p.kb_total + kbg) * kWTileBytes,
-                                      kWTileBytes, &fullb[stage], pol);
-                        else
-                            tma_load_2d_hint(w_tile(stage), &p.tm_w, &fullb[stage], kbg * 128, un.wt * 128, pol);
+                        const bool zp = C::ASYM && kbs == kb0;
+                        const uint32_t zb = zp ? (prepared ? static_cast<uint32_t>(g1 - g0) * 256u : C::GPU * 256u) : 0u;
+                        mbar_arrive_expect_tx(&fullb[stage], static_cast<uint32_t>(kn) * kWTileBytes + zb);
+                        if (prepared) {
+                            bulk_load(w_tile(stage), p.w_tiles + (static_cast<int64_t>(un.wt) * p.kb_total + kbs) * kWTileBytes,
+                                      static_cast<uint32_t>(kn) * kWTileBytes, &fullb[stage], pol);
+                        } else {
+                            for (int j = 0; j < kn; ++j)
+                                tma_load_2d_hint(w_tile(stage) + j * kWTileBytes, &p.tm_w, &fullb[stage], (kbs + j) * 128,
+                                                 un.wt * 128, pol);
+                        }
                         if (zp) {
                             if (prepared)
                                 bulk_load(w_zero(stage), p.wz_tiles + (static_cast<int64_t>(un.wt) * p.G + g0) * 256, zb,
                                           &fullb[stage], pol);
                             else
-                                tma_load_2d(w_zero(stage), &p.tm_wz, &fullb[stage], un.wt * 128, un.ut * C::GPK);
+                                tma_load_2d(w_zero(stage), &p.tm_wz, &fullb[stage], un.wt * 128, g0);
                         }
                     } else {
-                        mbar_arrive_expect_tx(&fullb[stage], static_cast<uint32_t>(C::A_STAGE));
-                        bulk_load(a_stage(stage), p.a_tiles + (static_cast<int64_t>(un.tt) * p.kb_total + kbg) * C::A_STAGE,
-                                  C::A_STAGE, &fullb[stage], pol);
+                        mbar_arrive_expect_tx(&fullb[stage], static_cast<uint32_t>(kn * C::A_TILE));
+                        bulk_load(a_stage(stage), p.a_tiles + (static_cast<int64_t>(un.tt) * p.kb_total + kbs) * C::A_TILE,
+                                  static_cast<uint32_t>(kn * C::A_TILE), &fullb[stage], pol);
                     }
                     ++issued;
                     if (++stage == ns) { stage = 0; ph ^= 1; }
@@ -508,9 +517,9 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         }
     } else if (warp <= kNumIssuers) {
         // ============================================================ MMA issuers
-        // Both issuers walk every k-block; issuer i issues the MMAs of the
+        // Both issuers walk every stage; issuer i issues the MMAs of the
         // accumulator slots whose global index is i mod 2, and both commit the
-        // k-block's TMEM A buffer and activation tile back (each covering its own MMAs).
+        // stage's TMEM A buffer and activation tiles back (each covering its own MMAs).
         const int me = warp - 1;
         if (elect_one()) {
             const uint32_t idesc = idesc_i8(128, TT);
@@ -522,31 +531,34 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 int kb0, kb1, g0, g1;
                 unit_kblocks<C>(p, un.ut, kb0, kb1);
                 unit_groups<C>(p, un.ut, g0, g1);
-                for (int kbg = kb0; kbg < kb1; ++kbg) {
+                for (int kbs = kb0; kbs < kb1; kbs += C::KS) {
+                    const int kn = min(C::KS, kb1 - kbs);
                     if (!mbar_wait(&bars->afull[sa], saph, abort_flag, p.status, kWMmaFull)) { ok = false; break; }
                     if (!mbar_wait(&bars->tfull[ab], abph, abort_flag, p.status, kWMmaAFull)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_smem = smem_u32(a_stage(sa));
-                    const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * 64);
+                    const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * C::ABUF);
                     if (C::GK <= 256) {
+                        // the unit is this one stage: groups g0..g1, CG per accumulator slot
                         for (int g = g0; g < g1; ++g) {
+                            const int gl = g - g0, gi = gl % C::CG;
                             const bool mine = (gsl & 1) == me;
-                            if (mine && (C::CG == 1 || g == g0)) {
+                            if (mine && gi == 0) {
                                 if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                                 tc_fence_after();
                             }
                             if (mine) {
-                                const uint32_t d_tmem = tbase + C::ACC0 +
-                                    static_cast<uint32_t>(sl * C::CG * TT + (C::CG == 1 ? 0 : (g - g0) * TT));
-                                const int ks0 = (g - g0) * (C::GK / 32);
+                                const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>((sl * C::CG + gi) * TT);
+                                const int j = gl / C::GPK;                       // k-block within the stage
+                                const int s0 = (gl % C::GPK) * (C::GK / 32);     // first K step within it
 #pragma unroll
-                                for (int j = 0; j < C::GK / 32; ++j) {
-                                    const int ks = ks0 + j;
-                                    const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
-                                    tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, 1u);
+                                for (int t = 0; t < C::GK / 32; ++t) {
+                                    const int ks = s0 + t;
+                                    const uint64_t bd = smem_desc_sw128(a_smem + j * C::A_TILE + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
+                                    tc_mma_i8_ts(d_tmem, a_tmem + j * 64 + ks * 8, bd, idesc, 1u);
                                 }
                             }
-                            if (C::CG == 1 || g == g1 - 1) {
+                            if (gi == C::CG - 1 || g == g1 - 1) {
                                 if (mine) tc_commit(&bars->accfull[sl]);
                                 ++gsl;
                                 if (++sl == C::NACC) { sl = 0; slph ^= 1; }
@@ -554,22 +566,26 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         }
                         if (!ok) break;
                     } else {
-                        const bool first = (kbg == kb0), last = (kbg == kb1 - 1);
+                        // one GK = 1024 group spread over several stages
                         const bool mine = (gsl & 1) == me;
+                        const bool first_stage = kbs == kb0, last_stage = kbs + kn >= kb1;
                         if (mine) {
-                            if (first) {
+                            if (first_stage) {
                                 if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                                 tc_fence_after();
                             }
                             const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>(sl * TT);
+                            for (int j = 0; j < kn; ++j) {
 #pragma unroll
-                            for (int ks = 0; ks < 8; ++ks) {
-                                const uint64_t bd = smem_desc_sw128(a_smem + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
-                                tc_mma_i8_ts(d_tmem, a_tmem + ks * 8, bd, idesc, (first && ks == 0) ? 0u : 1u);
+                                for (int ks = 0; ks < 8; ++ks) {
+                                    const uint64_t bd = smem_desc_sw128(a_smem + j * C::A_TILE + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
+                                    tc_mma_i8_ts(d_tmem, a_tmem + j * 64 + ks * 8, bd, idesc,
+                                                 (first_stage && j == 0 && ks == 0) ? 0u : 1u);
+                                }
                             }
-                            if (last) tc_commit(&bars->accfull[sl]);
+                            if (last_stage) tc_commit(&bars->accfull[sl]);
                         }
-                        if (last) {
+                        if (last_stage) {
                             ++gsl;
                             if (++sl == C::NACC) { sl = 0; slph ^= 1; }
                         }
@@ -586,54 +602,59 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         }
     } else if (warp < kNumPreWarps) {
         // ============================================================ converters
-        // Unpack one weight tile per k-block into a TMEM A buffer and hand the
-        // shared-memory tile straight back to the producer.
+        // Unpack one weight stage into a TMEM A buffer and hand the
+        // shared-memory tiles straight back to the producer.
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         int stage = 0, ab = 0;
         uint32_t sph = 0, abph = 0;
         bool ok = true;
-        uint32_t bias[C::GPK];
+        uint32_t bias[C::GPU];
 #pragma unroll
-        for (int i = 0; i < C::GPK; ++i) bias[i] = 0x78787878u;   // zero point 0
+        for (int i = 0; i < C::GPU; ++i) bias[i] = 0x78787878u;   // zero point 0
         Unit un = unit_of(p, u0);
         for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
             int kb0, kb1;
             unit_kblocks<C>(p, un.ut, kb0, kb1);
-            for (int kbg = kb0; kbg < kb1; ++kbg) {
+            for (int kbs = kb0; kbs < kb1; kbs += C::KS) {
+                const int kn = min(C::KS, kb1 - kbs);
                 if (!warp_wait(&bars->wfull[stage], sph, abort_flag, p.status, kWConvFull)) { ok = false; break; }
-                if (C::ASYM && kbg == kb0) {
+                if (C::ASYM && kbs == kb0) {
                     const uint16_t* wz = reinterpret_cast<const uint16_t*>(w_zero(stage));
 #pragma unroll
-                    for (int i = 0; i < C::GPK; ++i) {
+                    for (int i = 0; i < C::GPU; ++i) {
                         const int zu = static_cast<int>(bf16_bits_to_f32(wz[i * 128 + row])) + 8;
                         bias[i] = static_cast<uint32_t>((0x80 - zu) & 0xFF) * 0x01010101u;
                     }
                 }
                 if (!warp_wait(&bars->tempty[ab], abph ^ 1, abort_flag, p.status, kWConvAEmpty)) { ok = false; break; }
                 tc_fence_after();
-                const uint8_t* wrow = w_tile(stage) + row * 128;
-                const uint32_t a_tmem = tbase + lane_off + static_cast<uint32_t>(ab * 64);
+                const uint32_t a_tmem = tbase + lane_off + static_cast<uint32_t>(ab * C::ABUF);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
-                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                    uint32_t o[8];
-                    // chunk c holds K positions [32c, 32c+32) of this k-block
-                    const uint32_t bz = bias[C::GK <= 256 ? (c * 32) / (C::GK <= 256 ? C::GK : 256) : 0];
+                for (int j = 0; j < C::KS; ++j) {
+                    if (j >= kn) break;
+                    const uint8_t* wrow = w_tile(stage) + j * kWTileBytes + row * 128;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (C::SYM16) {
-                            o[2 * j] = (w[j] << 4) & 0xF0F0F0F0u;       // 16 * even-k weights
-                            o[2 * j + 1] = w[j] & 0xF0F0F0F0u;          // 16 * odd-k weights
-                        } else {
-                            const uint32_t x = w[j] ^ 0x88888888u;     // nibble + 8 in [0, 15]
-                            o[2 * j] = ((x & 0x0F0F0F0Fu) + bz) ^ 0x80808080u;
-                            o[2 * j + 1] = (((x >> 4) & 0x0F0F0F0Fu) + bz) ^ 0x80808080u;
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
+                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                        uint32_t o[8];
+                        // chunk c holds K positions [32c, 32c+32) of k-block j
+                        const uint32_t bz = bias[C::GK <= 256 ? j * C::GPK + (c * 32) / (C::GK <= 256 ? C::GK : 256) : 0];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            if (C::SYM16) {
+                                o[2 * q] = (w[q] << 4) & 0xF0F0F0F0u;       // 16 * even-k weights
+                                o[2 * q + 1] = w[q] & 0xF0F0F0F0u;          // 16 * odd-k weights
+                            } else {
+                                const uint32_t x = w[q] ^ 0x88888888u;     // nibble + 8 in [0, 15]
+                                o[2 * q] = ((x & 0x0F0F0F0Fu) + bz) ^ 0x80808080u;
+                                o[2 * q + 1] = (((x >> 4) & 0x0F0F0F0Fu) + bz) ^ 0x80808080u;
+                            }
                         }
+                        tc_st8(a_tmem + j * 64 + c * 8, o);
                     }
-                    tc_st8(a_tmem + c * 8, o);
                 }
                 tc_wait_st();
                 tc_fence_before();
