@@ -120,6 +120,7 @@ struct Bars {
     uint64_t tfull[4], tempty[4];       // converted weights in TMEM
     uint64_t accfull[8], accempty[8];   // accumulator slots
     uint64_t sfull[8], sempty[8];       // scale slots
+    uint64_t fin[2];                    // epilogue meeting points at the end of the range
     uint64_t drain[2];
     uint32_t tmem_base;
     int abort;
@@ -192,11 +193,6 @@ __device__ __forceinline__ int cta_of_unit(const GemmParams& p, int u, int C)
     return static_cast<int>((static_cast<int64_t>(u + 1) * C - 1) / p.total_units);
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads)
-{
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 // acc[j] += float(P_j) * (ws * as[j]) for NC consecutive columns, in packed
 // f32x2 arithmetic.  r holds the accumulator bits: 1.5*2^23 + P (MAGIC) or P.
 struct R16 {
@@ -238,42 +234,60 @@ __device__ __forceinline__ float acc_at(const uint64_t* acc2, int j)
 }
 
 // The last CTA to finish a split tile sums the parts in contributor order
-// (16 columns at a time, up to four contributors' loads in flight) and stores
-// the bf16 tile.  Kept out of line so its registers do not add to the
-// epilogue's steady-state loop.
+// and stores the bf16 tile.  Every contributor's part is located once, then
+// each 16-column chunk issues the loads of up to four contributors before
+// summing, so the tile costs about one L2 round trip per four contributors.
+// Kept out of line so its registers do not add to the epilogue's loop.
 template <int TT, int NC>
 __device__ __noinline__ void reduce_tile(const GemmParams& p, Unit un, int t, int cf, int cl, int nctas, int row,
                                          int col0, int ew, int lane)
 {
     const int n = un.wt * 128 + row;
     __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
-    for (int cc = 0; cc < NC; cc += 16) {
-        float sum[16];
+    float* park = nullptr;   // this tile's part of contributor cf: holds the running sum past four
+    for (int c2 = cf; c2 <= cl; c2 += 4) {
+        const float* src[4];
+        const int nq = min(4, cl - c2 + 1);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
-        for (int c2 = cf; c2 <= cl; c2 += 4) {
-            float v[4][16];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                if (c2 + q > cl) break;
+        for (int q = 0; q < 4; ++q) {
+            src[q] = p.partials;
+            if (q < nq) {
                 int cu0, cu1;
                 cta_range(p, c2 + q, nctas, cu0, cu1);
                 const int s2 = (t == cu0 / p.units_per_tile) ? 0 : 1;
-                const float* src = p.partials + static_cast<int64_t>(2 * (c2 + q) + s2) * (TT * 128);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[q][j] = __ldcg(src + (col0 + cc + j) * 128 + row);
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                if (c2 + q > cl) break;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) sum[j] += v[q][j];
+                src[q] = p.partials + static_cast<int64_t>(2 * (c2 + q) + s2) * (TT * 128) + row;
             }
         }
+        if (c2 == cf) park = const_cast<float*>(src[0]);
+        for (int cc = 0; cc < NC; cc += 16) {
+            float v[4][16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int m = un.tt * TT + col0 + cc + j;
-            if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[q][j] = q < nq ? __ldcg(src[q] + (col0 + cc + j) * 128) : 0.0f;
+            float sum[16];
+            if (c2 == cf) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sum[j] = __ldcg(park + (col0 + cc + j) * 128);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sum[j] += v[q][j];
+            if (c2 + 4 > cl) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int m = un.tt * TT + col0 + cc + j;
+                    if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
+                }
+            } else {
+                // more than four contributors: park the running sum in cf's part (already consumed)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) __stcg(park + (col0 + cc + j) * 128, sum[j]);
+            }
         }
     }
     if (ew == 0 && lane == 0) p.counters[t] = 0;
@@ -310,12 +324,22 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v)
     return old;
 }
 
+// The epilogue warps meet on `bar` (phase `parity`).  Bounded: a warp that
+// gave up never arrives, and the others then give up too instead of hanging.
+__device__ __forceinline__ bool epi_meet(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                         int lane)
+{
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+    return warp_wait(bar, parity, abort_flag, status, kWDrain);
+}
+
 // End of a CTA's share of one output tile: store it, or store the partial and
 // announce it with one release/acquire atomic whose answer is consumed later.
 template <class C>
-__device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, int u0, int u1, int cta, int nctas,
-                                           int row, int col0, int ew, int lane, int nthr,
-                                           const uint64_t (&acc2)[C::NC / 2], Pending& pend)
+__device__ __forceinline__ bool flush_tile(const GemmParams& p, const Unit& un, int u0, int u1, int cta, int nctas,
+                                           int row, int col0, int ew, int lane, const uint64_t (&acc2)[C::NC / 2],
+                                           Pending& pend, int npend, Bars* bars, volatile int* abort_flag)
 {
     constexpr int TT = C::TT, NC = C::NC;
     const int t = un.t;
@@ -328,35 +352,38 @@ __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, 
             const int m = un.tt * TT + col0 + j;
             if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(acc_at(acc2, j));
         }
-        return;
+        return true;
     }
     const int side = (t == u0 / p.units_per_tile) ? 0 : 1;
     float* mine = p.partials + static_cast<int64_t>(2 * cta + side) * (TT * 128);
 #pragma unroll
     for (int j = 0; j < NC; ++j) __stcg(mine + (col0 + j) * 128 + row, acc_at(acc2, j));
-    named_bar_sync(1, nthr);     // every epilogue thread's part is written (CTA-scope order)
+    // every epilogue thread's part is written (CTA-scope order) before the release
+    if (!epi_meet(&bars->fin[0], static_cast<uint32_t>(npend & 1), abort_flag, p.status, lane)) return false;
     pend.un = un;
     pend.cf = cta_of_unit(p, tfirst, nctas);
     pend.cl = cta_of_unit(p, tlast, nctas);
     pend.valid = 1;
-    // Release (cumulative over the barrier above) publishes the part; acquire
+    // Release (cumulative over the meeting above) publishes the part; acquire
     // lets a last arriver see every other part.  The result is only read at
     // the end of the CTA, so the round trip overlaps the rest of the work.
     if (ew == 0 && lane == 0) pend.old = atom_add_acq_rel_gpu(&p.counters[t], 1);
+    return true;
 }
 
 // After the CTA's last unit: reduce the split tiles this CTA arrived last at.
 template <class C>
 __device__ __forceinline__ void finish_pending(const GemmParams& p, int nctas, int row, int col0, int ew, int lane,
-                                               int nthr, Pending (&pend)[2], Bars* bars)
+                                               Pending (&pend)[2], Bars* bars, volatile int* abort_flag)
 {
+    if (!pend[0].valid && !pend[1].valid) return;       // the same in every epilogue thread
     if (ew == 0 && lane == 0) {
         bars->last_flag = 0;
 #pragma unroll
         for (int i = 0; i < 2; ++i)
             if (pend[i].valid && pend[i].old == pend[i].cl - pend[i].cf) bars->last_flag |= 1 << i;
     }
-    named_bar_sync(1, nthr);
+    if (!epi_meet(&bars->fin[1], 0, abort_flag, p.status, lane)) return;
     const int flags = bars->last_flag;
 #pragma unroll
     for (int i = 0; i < 2; ++i)
@@ -394,11 +421,11 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         }
         for (int i = 0; i < C::S_A; ++i) {
             mbar_init(&bars->afull[i], 1);                  // activation producer (+ bytes)
-            mbar_init(&bars->aempty[i], kNumIssuers);       // each issuer's commit
+            mbar_init(&bars->aempty[i], 1);                 // the owning issuer's commit
         }
         for (int i = 0; i < C::NA; ++i) {
             mbar_init(&bars->tfull[i], 4);
-            mbar_init(&bars->tempty[i], kNumIssuers);
+            mbar_init(&bars->tempty[i], 1);
         }
         for (int i = 0; i < C::NACC; ++i) {
             mbar_init(&bars->accfull[i], 1);
@@ -408,6 +435,8 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             mbar_init(&bars->sfull[i], 1);                  // activation producer (+ bytes)
             mbar_init(&bars->sempty[i], 4 * C::E);          // epilogue warps
         }
+        mbar_init(&bars->fin[0], 4 * C::E);
+        mbar_init(&bars->fin[1], 4 * C::E);
         mbar_init(&bars->drain[0], 1);
         mbar_init(&bars->drain[1], 1);
         bars->abort = 0;
@@ -517,13 +546,15 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         }
     } else if (warp <= kNumIssuers) {
         // ============================================================ MMA issuers
-        // Both issuers walk every stage; issuer i issues the MMAs of the
-        // accumulator slots whose global index is i mod 2, and both commit the
-        // stage's TMEM A buffer and activation tiles back (each covering its own MMAs).
+        // Issuer i owns the units u0 + i, u0 + i + 2, ...: for those it waits
+        // for the stages, issues every MMA and commits the stages' buffers and
+        // the unit's accumulator slots; for the other issuer's units it only
+        // advances its ring positions.  Each barrier hand-over costs a few
+        // hundred cycles, so splitting whole units halves every issuer's share.
         const int me = warp - 1;
         if (elect_one()) {
             const uint32_t idesc = idesc_i8(128, TT);
-            int sa = 0, ab = 0, sl = 0, gsl = 0;
+            int sa = 0, ab = 0, sl = 0;
             uint32_t saph = 0, abph = 0, slph = 0;
             bool ok = true;
             Unit un = unit_of(p, u0);
@@ -531,23 +562,23 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 int kb0, kb1, g0, g1;
                 unit_kblocks<C>(p, un.ut, kb0, kb1);
                 unit_groups<C>(p, un.ut, g0, g1);
+                const bool mine = ((u - u0) & 1) == me;
                 for (int kbs = kb0; kbs < kb1; kbs += C::KS) {
                     const int kn = min(C::KS, kb1 - kbs);
-                    if (!mbar_wait(&bars->afull[sa], saph, abort_flag, p.status, kWMmaFull)) { ok = false; break; }
-                    if (!mbar_wait(&bars->tfull[ab], abph, abort_flag, p.status, kWMmaAFull)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t a_smem = smem_u32(a_stage(sa));
-                    const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * C::ABUF);
-                    if (C::GK <= 256) {
-                        // the unit is this one stage: groups g0..g1, CG per accumulator slot
-                        for (int g = g0; g < g1; ++g) {
-                            const int gl = g - g0, gi = gl % C::CG;
-                            const bool mine = (gsl & 1) == me;
-                            if (mine && gi == 0) {
-                                if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
-                                tc_fence_after();
-                            }
-                            if (mine) {
+                    if (mine) {
+                        if (!mbar_wait(&bars->afull[sa], saph, abort_flag, p.status, kWMmaFull)) { ok = false; break; }
+                        if (!mbar_wait(&bars->tfull[ab], abph, abort_flag, p.status, kWMmaAFull)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t a_smem = smem_u32(a_stage(sa));
+                        const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * C::ABUF);
+                        if (C::GK <= 256) {
+                            // the unit is this one stage: groups g0..g1, CG per accumulator slot
+                            for (int g = g0; g < g1; ++g) {
+                                const int gl = g - g0, gi = gl % C::CG;
+                                if (gi == 0) {
+                                    if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                                    tc_fence_after();
+                                }
                                 const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>((sl * C::CG + gi) * TT);
                                 const int j = gl / C::GPK;                       // k-block within the stage
                                 const int s0 = (gl % C::GPK) * (C::GK / 32);     // first K step within it
@@ -557,19 +588,15 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                                     const uint64_t bd = smem_desc_sw128(a_smem + j * C::A_TILE + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
                                     tc_mma_i8_ts(d_tmem, a_tmem + j * 64 + ks * 8, bd, idesc, 1u);
                                 }
+                                if (gi == C::CG - 1 || g == g1 - 1) {
+                                    tc_commit(&bars->accfull[sl]);
+                                    if (++sl == C::NACC) { sl = 0; slph ^= 1; }
+                                }
                             }
-                            if (gi == C::CG - 1 || g == g1 - 1) {
-                                if (mine) tc_commit(&bars->accfull[sl]);
-                                ++gsl;
-                                if (++sl == C::NACC) { sl = 0; slph ^= 1; }
-                            }
-                        }
-                        if (!ok) break;
-                    } else {
-                        // one GK = 1024 group spread over several stages
-                        const bool mine = (gsl & 1) == me;
-                        const bool first_stage = kbs == kb0, last_stage = kbs + kn >= kb1;
-                        if (mine) {
+                            if (!ok) break;
+                        } else {
+                            // one GK = 1024 group spread over several stages
+                            const bool first_stage = kbs == kb0, last_stage = kbs + kn >= kb1;
                             if (first_stage) {
                                 if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                                 tc_fence_after();
@@ -583,15 +610,19 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                                                  (first_stage && j == 0 && ks == 0) ? 0u : 1u);
                                 }
                             }
-                            if (last_stage) tc_commit(&bars->accfull[sl]);
+                            if (last_stage) {
+                                tc_commit(&bars->accfull[sl]);
+                                if (++sl == C::NACC) { sl = 0; slph ^= 1; }
+                            }
                         }
-                        if (last_stage) {
-                            ++gsl;
+                        tc_commit(&bars->tempty[ab]);
+                        tc_commit(&bars->aempty[sa]);
+                    } else {
+                        // the other issuer's stage: keep the slot position in step
+                        const int nslots = C::GK <= 256 ? (g1 - g0 + C::CG - 1) / C::CG : (kbs + kn >= kb1 ? 1 : 0);
+                        for (int i = 0; i < nslots; ++i)
                             if (++sl == C::NACC) { sl = 0; slph ^= 1; }
-                        }
                     }
-                    tc_commit(&bars->tempty[ab]);
-                    tc_commit(&bars->aempty[sa]);
                     if (++ab == C::NA) { ab = 0; abph ^= 1; }
                     if (++sa == C::S_A) { sa = 0; saph ^= 1; }
                 }
@@ -677,7 +708,6 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         const int col0 = part * C::NC;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         constexpr int NCH = C::NCH;
-        const int nthr = 4 * C::E * 32;
 
         if (C::MAGIC) {
             for (int b = 0; b < C::NACC; ++b)
@@ -764,14 +794,15 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             // ---- end of this CTA's share of tile t: store or hand over ----
             if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
                 if (!out_partials) {
-                    flush_tile<C>(p, un, u0, u1, cta, nctas, row, col0, ew, lane, nthr, acc2, pend[npend]);
+                    if (!flush_tile<C>(p, un, u0, u1, cta, nctas, row, col0, ew, lane, acc2, pend[npend], npend, bars,
+                                       abort_flag)) { ok = false; break; }
                     if (pend[npend].valid && npend < 1) ++npend;
                 }
 #pragma unroll
                 for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
             }
         }
-        if (!out_partials) finish_pending<C>(p, nctas, row, col0, ew, lane, nthr, pend, bars);
+        if (!out_partials) finish_pending<C>(p, nctas, row, col0, ew, lane, pend, bars, abort_flag);
     }
 
     // ---------------------------------------------------------------- teardown
