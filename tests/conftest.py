@@ -6,8 +6,9 @@ import numpy as np
 import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TESTS = os.path.dirname(os.path.abspath(__file__))
 PKG_ROOT = os.path.join(REPO, "vllm-ascend910_b200")
-for p in (REPO, PKG_ROOT):
+for p in (REPO, PKG_ROOT, TESTS):
     if p not in sys.path:
         sys.path.insert(0, p)
 

@@ -1,0 +1,262 @@
+"""Tensor-parallel QwQ-32B decoder-layer linear stack on W4A8 linears.
+
+Per layer (the reference's fused-layer benchmark, npu_ops/python/bench_fused_layer.py:63-66;
+vLLM's Column/RowParallelLinear sharding):
+
+    qkv     column-parallel  [M, H]      -> [M, QKV/tp]  (q, k and v sections each split, as
+                                                         vLLM's QKVParallelLinear does)
+    att     the rank's q section, H/tp columns (an attention stand-in: the stack has no
+            attention; with per-section shards it is the same map at every tp)
+    o_proj  row-parallel     [M, H/tp]   -> [M, H] partial   -> all-reduce
+    gate_up column-parallel  [M, H]      -> [M, 2F/tp]  ([gate_shard; up_shard] rows, vLLM's
+                                                         MergedColumnParallelLinear order)
+    act     silu(gate) * up              -> [M, F/tp]
+    down    row-parallel     [M, F/tp]   -> [M, H] partial   -> all-reduce
+
+Row-parallel shards split K at group boundaries (H/tp and F/tp are multiples of the group
+size for every tp <= 8 at GK = 128), so each rank's scales are the [G/tp, N] slice.  All
+ranks draw the full weights from the same seed and keep their shard, so any tp gives the
+same layer as tp = 1 up to the order of the bf16 all-reduce.
+
+The forward takes the linear and all-reduce as callables: the product uses the CUDA op on
+prepared weights and NCCL; the CPU tests pass reference arithmetic and gloo.
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Callable, Dict, List, Optional, Sequence
+
+import torch
+
+GK = 128
+
+
+@dataclasses.dataclass(frozen=True)
+class Dims:
+    hidden: int = 5120
+    qkv: int = 7168
+    ffn: int = 27648
+    gk: int = GK
+
+
+QWQ = Dims()
+
+
+@dataclasses.dataclass
+class ShardWeights:
+    """One linear's shard: int8 codes [N, K] (kept for checking), the packed layout and scales."""
+    codes: torch.Tensor
+    packed: torch.Tensor
+    scale: torch.Tensor        # [G, N] fp32
+    K: int
+    N: int
+    prepared: Optional[object] = None
+
+
+@dataclasses.dataclass
+class LayerShard:
+    qkv: ShardWeights
+    o: ShardWeights
+    gate_up: ShardWeights
+    down: ShardWeights
+
+
+def check_dims(d: Dims, tp: int) -> None:
+    for name, k in (("hidden", d.hidden), ("ffn", d.ffn)):
+        if k % (tp * d.gk):
+            raise ValueError(f"{name}={k} does not split into {tp} group-aligned shards of GK={d.gk}")
+    for name, n in (("qkv", d.qkv), ("ffn", d.ffn)):
+        if n % (tp * 8):
+            raise ValueError(f"{name}={n} does not split into {tp} output shards of a multiple of 8")
+    kv = (d.qkv - d.hidden) // 2
+    if d.qkv <= d.hidden or (d.qkv - d.hidden) % 2 or kv % (tp * 8):
+        raise ValueError(f"qkv={d.qkv} is not q={d.hidden} plus two kv sections that split {tp} ways")
+
+
+def _full(N: int, K: int, gk: int, gen: torch.Generator, device):
+    G = -(-K // gk)
+    codes = torch.randint(-8, 8, (N, K), generator=gen, device=device, dtype=torch.int16).to(torch.int8)
+    scale = torch.exp(torch.randn(G, N, generator=gen, device=device) * 0.5 - 6.0)
+    return codes, scale
+
+
+def _make(codes: torch.Tensor, scale: torch.Tensor, gk: int, device) -> ShardWeights:
+    from . import ops
+    codes = codes.to(device).contiguous()
+    scale = scale.to(device)
+    return ShardWeights(codes=codes, packed=ops.pack_int4_grouped(codes, gk), scale=scale.contiguous(),
+                        K=codes.shape[1], N=codes.shape[0])
+
+
+def column_shard(codes: torch.Tensor, scale: torch.Tensor, rank: int, tp: int):
+    """Rows [rank*N/tp, (rank+1)*N/tp) of the output dimension."""
+    n = codes.shape[0] // tp
+    return codes[rank * n:(rank + 1) * n], scale[:, rank * n:(rank + 1) * n]
+
+
+def sections_shard(codes: torch.Tensor, scale: torch.Tensor, rank: int, tp: int, sizes: Sequence[int]):
+    """The rank's rows of each output section, concatenated in section order (vLLM's
+    MergedColumnParallelLinear [gate; up] and QKVParallelLinear [q; k; v])."""
+    cs, ss, n0 = [], [], 0
+    for n in sizes:
+        c, sc = column_shard(codes[n0:n0 + n], scale[:, n0:n0 + n], rank, tp)
+        cs.append(c)
+        ss.append(sc)
+        n0 += n
+    return torch.cat(cs, 0), torch.cat(ss, 1)
+
+
+def merged_column_shard(codes: torch.Tensor, scale: torch.Tensor, rank: int, tp: int):
+    """[gate_shard; up_shard] of a [gate; up] weight."""
+    f = codes.shape[0] // 2
+    return sections_shard(codes, scale, rank, tp, (f, f))
+
+
+def qkv_shard(codes: torch.Tensor, scale: torch.Tensor, rank: int, tp: int, hidden: int):
+    """[q_shard; k_shard; v_shard] of a [q; k; v] weight with q = hidden rows."""
+    kv = (codes.shape[0] - hidden) // 2
+    return sections_shard(codes, scale, rank, tp, (hidden, kv, kv))
+
+
+def row_shard(codes: torch.Tensor, scale: torch.Tensor, rank: int, tp: int, gk: int):
+    """Columns [rank*K/tp, (rank+1)*K/tp) of the input dimension and their scale groups."""
+    k = codes.shape[1] // tp
+    g = k // gk
+    return codes[:, rank * k:(rank + 1) * k], scale[rank * g:(rank + 1) * g]
+
+
+def build_layers(n_layers: int, rank: int, tp: int, device, d: Dims = QWQ, seed: int = 1234,
+                 prepare: bool = False, gen_device=None) -> List[LayerShard]:
+    """Each rank draws the full layer weights from `seed` and keeps its shard.
+
+    The draw happens on `gen_device` (default `device`): torch's CPU and CUDA
+    generators give different streams, so ranks must draw on the same kind of
+    device to hold shards of one layer."""
+    check_dims(d, tp)
+    out = []
+    gdev = device if gen_device is None else gen_device
+    gen = torch.Generator(device=gdev).manual_seed(seed)
+    for _ in range(n_layers):
+        qkv_c, qkv_s = _full(d.qkv, d.hidden, d.gk, gen, gdev)
+        o_c, o_s = _full(d.hidden, d.hidden, d.gk, gen, gdev)
+        gu_c, gu_s = _full(2 * d.ffn, d.hidden, d.gk, gen, gdev)
+        dn_c, dn_s = _full(d.hidden, d.ffn, d.gk, gen, gdev)
+        L = LayerShard(qkv=_make(*qkv_shard(qkv_c, qkv_s, rank, tp, d.hidden), d.gk, device),
+                       o=_make(*row_shard(o_c, o_s, rank, tp, d.gk), d.gk, device),
+                       gate_up=_make(*merged_column_shard(gu_c, gu_s, rank, tp), d.gk, device),
+                       down=_make(*row_shard(dn_c, dn_s, rank, tp, d.gk), d.gk, device))
+        del qkv_c, o_c, gu_c, dn_c
+        if prepare:
+            from . import ops
+            for w in (L.qkv, L.o, L.gate_up, L.down):
+                w.prepared = ops.prepare_weights(w.packed, w.scale, None, w.K, d.gk)
+        out.append(L)
+    return out
+
+
+Linear = Callable[[torch.Tensor, ShardWeights], torch.Tensor]
+AllReduce = Callable[[torch.Tensor], None]
+
+
+def cuda_linear(x: torch.Tensor, w: ShardWeights) -> torch.Tensor:
+    from . import ops
+    if w.prepared is not None:
+        return ops.linear_prepared(x, w.prepared)
+    return ops.linear(x, w.packed, w.scale, None, GK)
+
+
+def layer_forward(h: torch.Tensor, L: LayerShard, tp: int, linear: Linear, allreduce: AllReduce,
+                  d: Dims = QWQ) -> torch.Tensor:
+    qkv = linear(h, L.qkv)
+    att = qkv[:, : d.hidden // tp]                     # attention stand-in: the rank's q section
+    o = linear(att, L.o)
+    allreduce(o)
+    gu = linear(o, L.gate_up)
+    f = d.ffn // tp
+    act = (torch.nn.functional.silu(gu[:, :f].float()) * gu[:, f:].float()).to(torch.bfloat16)
+    dn = linear(act, L.down)
+    allreduce(dn)
+    return dn
+
+
+def stack_forward(h: torch.Tensor, layers: Sequence[LayerShard], tp: int, linear: Linear,
+                  allreduce: AllReduce, d: Dims = QWQ) -> torch.Tensor:
+    for L in layers:
+        h = layer_forward(h, L, tp, linear, allreduce, d)
+    return h
+
+
+def nccl_allreduce(group=None) -> AllReduce:
+    import torch.distributed as dist
+
+    def f(t: torch.Tensor) -> None:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return f
+
+
+def _roofline_seconds(layers: Sequence[LayerShard], M: int, hbm_gbs: float, i8_tops: Optional[float]) -> float:
+    """Per-rank lower bound: each GEMM at the slower of its HBM and int8 bounds."""
+    t = 0.0
+    for L in layers:
+        for w in (L.qkv, L.o, L.gate_up, L.down):
+            G = -(-w.K // GK)
+            by = w.N * w.K // 2 + G * w.N * 4 + M * w.K * 2 + M * w.N * 2
+            t_mem = by / (hbm_gbs * 1e9)
+            t_ops = 2.0 * M * w.N * w.K / (i8_tops * 1e12) if i8_tops else 0.0
+            t += max(t_mem, t_ops)
+    return t
+
+
+def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4, iters: int = 10,
+                hbm_gbs: float = 6556.5, i8_tops: Optional[float] = None) -> Dict:
+    """Time `layers` sharded layers at each M on `world` GPUs (one rank each).
+
+    The step is captured in a CUDA graph (NCCL included); the time is the max
+    over ranks of CUDA-event time per forward.  Returns tokens/s (M per forward)
+    and layer-tokens/s (M x layers per forward) with the roofline fraction."""
+    import torch.distributed as dist
+    d = QWQ
+    Ls = build_layers(layers, rank, world, dev, d, prepare=True)
+    ar = nccl_allreduce() if world > 1 else (lambda t: None)
+    res = []
+    for M in ms:
+        gen = torch.Generator(device=dev).manual_seed(99 + M)
+        h0 = torch.randn(M, d.hidden, generator=gen, device=dev).to(torch.bfloat16)
+
+        def fwd():
+            return stack_forward(h0, Ls, world, cuda_linear, ar, d)
+
+        for _ in range(2):
+            fwd()
+        torch.cuda.synchronize()
+        graph = None
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fwd()
+        except Exception:
+            graph = None
+        run = graph.replay if graph is not None else fwd
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e-3 / iters
+        if world > 1:
+            tt = torch.tensor([t], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        roof = _roofline_seconds(Ls, M, hbm_gbs, i8_tops)
+        res.append({"M": M, "ms_per_forward": 1e3 * t, "tokens_per_s": M / t,
+                    "layer_tokens_per_s": M * layers / t, "roofline_frac": roof / t,
+                    "graph": graph is not None})
+        del graph
+    return {"tp": world, "layers": layers, "dims": dataclasses.asdict(d), "per_M": res,
+            "note": "attention replaced by the first hidden/tp columns of the QKV output"}
