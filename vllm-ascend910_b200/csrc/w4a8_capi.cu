@@ -92,6 +92,7 @@ struct Plan {
     int64_t M, N, K, Kpad, G;
     int gk, tt, n_wt, n_tt, upt, units, grid, kb_total;
     size_t off_counters, off_as, off_aq, off_part, total;
+    bool split;   // some output tile's units are divided between CTAs
 };
 
 Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
@@ -113,6 +114,9 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
     p.upt = gk <= 256 ? static_cast<int>(cdiv(p.kb_total, ks)) : static_cast<int>(p.G);
     p.units = p.n_wt * p.n_tt * p.upt;
     p.grid = std::max(1, std::min(sms, p.units));
+    p.split = false;
+    for (int c = 1; c < p.grid && !p.split; ++c)
+        p.split = (static_cast<int64_t>(c) * p.units / p.grid) % p.upt != 0;
     size_t off = 256;                                                     // status word block
     p.off_counters = off;
     off += round_up(static_cast<int64_t>(p.n_wt) * p.n_tt * 4, 256);
@@ -286,7 +290,9 @@ int run_gemm(const Plan& pl, const Weights& w, void* out, int64_t ldy, bool part
     c.asym = asym;
     c.ws_bf16 = w.ws_dtype != W4A8_DTYPE_F32;
     c.partials = partials;
-    const cudaError_t e = launch_gemm(g, c, pl.grid, st, true);
+    cudaError_t e = launch_gemm(g, c, pl.grid, st, true);
+    if (e != cudaSuccess) return fail_cuda(e);
+    if (!partials && pl.split) e = launch_splitk_reduce(g, pl.tt, pl.grid, st);
     return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
 }
 

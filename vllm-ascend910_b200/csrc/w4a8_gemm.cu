@@ -120,11 +120,9 @@ struct Bars {
     uint64_t tfull[4], tempty[4];       // converted weights in TMEM
     uint64_t accfull[8], accempty[8];   // accumulator slots
     uint64_t sfull[8], sempty[8];       // scale slots
-    uint64_t fin[2];                    // epilogue meeting points at the end of the range
     uint64_t drain[2];
     uint32_t tmem_base;
     int abort;
-    int last_flag;
 };
 
 static_assert(sizeof(Bars) <= kBarBytes, "barrier block overflows its reservation");
@@ -233,66 +231,6 @@ __device__ __forceinline__ float acc_at(const uint64_t* acc2, int j)
     return __uint_as_float(static_cast<uint32_t>(acc2[j >> 1] >> ((j & 1) * 32)));
 }
 
-// The last CTA to finish a split tile sums the parts in contributor order
-// and stores the bf16 tile.  Every contributor's part is located once, then
-// each 16-column chunk issues the loads of up to four contributors before
-// summing, so the tile costs about one L2 round trip per four contributors.
-// Kept out of line so its registers do not add to the epilogue's loop.
-template <int TT, int NC>
-__device__ __noinline__ void reduce_tile(const GemmParams& p, Unit un, int t, int cf, int cl, int nctas, int row,
-                                         int col0, int ew, int lane)
-{
-    const int n = un.wt * 128 + row;
-    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
-    float* park = nullptr;   // this tile's part of contributor cf: holds the running sum past four
-    for (int c2 = cf; c2 <= cl; c2 += 4) {
-        const float* src[4];
-        const int nq = min(4, cl - c2 + 1);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            src[q] = p.partials;
-            if (q < nq) {
-                int cu0, cu1;
-                cta_range(p, c2 + q, nctas, cu0, cu1);
-                const int s2 = (t == cu0 / p.units_per_tile) ? 0 : 1;
-                src[q] = p.partials + static_cast<int64_t>(2 * (c2 + q) + s2) * (TT * 128) + row;
-            }
-        }
-        if (c2 == cf) park = const_cast<float*>(src[0]);
-        for (int cc = 0; cc < NC; cc += 16) {
-            float v[4][16];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[q][j] = q < nq ? __ldcg(src[q] + (col0 + cc + j) * 128) : 0.0f;
-            float sum[16];
-            if (c2 == cf) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) sum[j] = __ldcg(park + (col0 + cc + j) * 128);
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int j = 0; j < 16; ++j) sum[j] += v[q][j];
-            if (c2 + 4 > cl) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int m = un.tt * TT + col0 + cc + j;
-                    if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
-                }
-            } else {
-                // more than four contributors: park the running sum in cf's part (already consumed)
-#pragma unroll
-                for (int j = 0; j < 16; ++j) __stcg(park + (col0 + cc + j) * 128, sum[j]);
-            }
-        }
-    }
-    if (ew == 0 && lane == 0) p.counters[t] = 0;
-}
-
 // Debug output mode: the exact int32 partials of one 16-column chunk of group g.
 template <bool MAGIC, bool SYM16>
 __device__ __noinline__ void store_partials(const GemmParams& p, R16 r, int g, int m0, int n)
@@ -307,88 +245,30 @@ __device__ __noinline__ void store_partials(const GemmParams& p, R16 r, int g, i
     }
 }
 
-// A split tile this CTA contributed to, remembered until the end of the CTA's
-// range, when the arrival count returned by its release/acquire atomic says
-// whether this CTA was the last contributor (and so reduces the tile).
-struct Pending {
-    Unit un;
-    int cf, cl;
-    int old;     // arrival count before this CTA's arrival (meaningful in the electing thread)
-    int valid;
-};
-
-__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v)
-{
-    int old;
-    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
-    return old;
-}
-
-// The epilogue warps meet on `bar` (phase `parity`).  Bounded: a warp that
-// gave up never arrives, and the others then give up too instead of hanging.
-__device__ __forceinline__ bool epi_meet(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                         int lane)
-{
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar);
-    return warp_wait(bar, parity, abort_flag, status, kWDrain);
-}
-
-// End of a CTA's share of one output tile: store it, or store the partial and
-// announce it with one release/acquire atomic whose answer is consumed later.
+// End of a CTA's share of one output tile: store the bf16 tile when the CTA
+// computed all of it, else store its fp32 part for w4a8_splitk_reduce_kernel
+// (which runs after the GEMM, so no fence or arrival count is needed here).
 template <class C>
-__device__ __forceinline__ bool flush_tile(const GemmParams& p, const Unit& un, int u0, int u1, int cta, int nctas,
-                                           int row, int col0, int ew, int lane, const uint64_t (&acc2)[C::NC / 2],
-                                           Pending& pend, int npend, Bars* bars, volatile int* abort_flag)
+__device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, int u0, int u1, int cta, int row,
+                                           int col0, const uint64_t (&acc2)[C::NC / 2])
 {
     constexpr int TT = C::TT, NC = C::NC;
     const int t = un.t;
     const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
     const int n = un.wt * 128 + row;
-    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
     if (u0 <= tfirst && u1 - 1 >= tlast) {
+        __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
         for (int j = 0; j < NC; ++j) {
             const int m = un.tt * TT + col0 + j;
             if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(acc_at(acc2, j));
         }
-        return true;
+        return;
     }
     const int side = (t == u0 / p.units_per_tile) ? 0 : 1;
     float* mine = p.partials + static_cast<int64_t>(2 * cta + side) * (TT * 128);
 #pragma unroll
     for (int j = 0; j < NC; ++j) __stcg(mine + (col0 + j) * 128 + row, acc_at(acc2, j));
-    // every epilogue thread's part is written (CTA-scope order) before the release
-    if (!epi_meet(&bars->fin[0], static_cast<uint32_t>(npend & 1), abort_flag, p.status, lane)) return false;
-    pend.un = un;
-    pend.cf = cta_of_unit(p, tfirst, nctas);
-    pend.cl = cta_of_unit(p, tlast, nctas);
-    pend.valid = 1;
-    // Release (cumulative over the meeting above) publishes the part; acquire
-    // lets a last arriver see every other part.  The result is only read at
-    // the end of the CTA, so the round trip overlaps the rest of the work.
-    if (ew == 0 && lane == 0) pend.old = atom_add_acq_rel_gpu(&p.counters[t], 1);
-    return true;
-}
-
-// After the CTA's last unit: reduce the split tiles this CTA arrived last at.
-template <class C>
-__device__ __forceinline__ void finish_pending(const GemmParams& p, int nctas, int row, int col0, int ew, int lane,
-                                               Pending (&pend)[2], Bars* bars, volatile int* abort_flag)
-{
-    if (!pend[0].valid && !pend[1].valid) return;       // the same in every epilogue thread
-    if (ew == 0 && lane == 0) {
-        bars->last_flag = 0;
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-            if (pend[i].valid && pend[i].old == pend[i].cl - pend[i].cf) bars->last_flag |= 1 << i;
-    }
-    if (!epi_meet(&bars->fin[1], 0, abort_flag, p.status, lane)) return;
-    const int flags = bars->last_flag;
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-        if (flags & (1 << i))
-            reduce_tile<C::TT, C::NC>(p, pend[i].un, pend[i].un.t, pend[i].cf, pend[i].cl, nctas, row, col0, ew, lane);
 }
 
 template <int TT, int GK, bool ASYM>
@@ -435,8 +315,6 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             mbar_init(&bars->sfull[i], 1);                  // activation producer (+ bytes)
             mbar_init(&bars->sempty[i], 4 * C::E);          // epilogue warps
         }
-        mbar_init(&bars->fin[0], 4 * C::E);
-        mbar_init(&bars->fin[1], 4 * C::E);
         mbar_init(&bars->drain[0], 1);
         mbar_init(&bars->drain[1], 1);
         bars->abort = 0;
@@ -727,10 +605,6 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         uint64_t acc2[C::NC / 2];
 #pragma unroll
         for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
-        Pending pend[2];
-        pend[0].valid = pend[1].valid = 0;
-        pend[0].old = pend[1].old = -1;
-        int npend = 0;
         int sl = 0, slot = 0;
         uint32_t aph = 0, slph = 0;
         bool ok = true;
@@ -794,15 +668,12 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             // ---- end of this CTA's share of tile t: store or hand over ----
             if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
                 if (!out_partials) {
-                    if (!flush_tile<C>(p, un, u0, u1, cta, nctas, row, col0, ew, lane, acc2, pend[npend], npend, bars,
-                                       abort_flag)) { ok = false; break; }
-                    if (pend[npend].valid && npend < 1) ++npend;
+                    flush_tile<C>(p, un, u0, u1, cta, row, col0, acc2);
                 }
 #pragma unroll
                 for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
             }
         }
-        if (!out_partials) finish_pending<C>(p, nctas, row, col0, ew, lane, pend, bars, abort_flag);
     }
 
     // ---------------------------------------------------------------- teardown
@@ -855,6 +726,58 @@ __global__ void prepare_weights_kernel(const PrepareParams p)
             if (p.w_zero)
                 reinterpret_cast<uint16_t*>(p.out + L.off_wz)[j] =
                     in ? p.w_zero[static_cast<int64_t>(g) * p.N + n] : 0;
+        }
+    }
+}
+
+// Stream-K fix-up: one block per 16-token column chunk of an output tile
+// (128 weight rows x TT tokens).
+// A tile whose units were split across CTAs c_first..c_last is summed from
+// their fp32 parts in CTA order (deterministic) and stored as bf16; tiles a
+// single CTA finished were stored by the GEMM and are skipped.  Launched
+// right after the GEMM as a programmatic dependent: it waits for the GEMM
+// grid to complete, so every part is visible without fences.
+template <int TT>
+__global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, const int nctas)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x;
+    const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
+    const int cf = cta_of_unit(p, tfirst, nctas), cl = cta_of_unit(p, tlast, nctas);
+    if (cf == cl) return;
+    const int wt = t / p.n_tt, tt = t - wt * p.n_tt;
+    const int row = threadIdx.x;
+    const int n = wt * 128 + row;
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
+    {
+        const int c0 = blockIdx.y * 16;
+        float sum[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+        for (int c = cf; c <= cl; c += 4) {
+            float v[4][16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float* src = p.partials;
+                bool valid = c + q <= cl;
+                if (valid) {
+                    int u0, u1;
+                    cta_range(p, c + q, nctas, u0, u1);
+                    src = p.partials + static_cast<int64_t>(2 * (c + q) + (t == u0 / p.units_per_tile ? 0 : 1)) * (TT * 128);
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[q][j] = valid ? __ldcg(src + (c0 + j) * 128 + row) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sum[j] += v[q][j];
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int m = tt * TT + c0 + j;
+            if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
         }
     }
 }
@@ -927,6 +850,27 @@ cudaError_t launch_gemm(const GemmParams& p, const GemmConfig& c, int grid, cuda
         case 32: return launch_tt<32>(p, c, grid, stream, pdl);
         case 64: return launch_tt<64>(p, c, grid, stream, pdl);
         case 128: return launch_tt<128>(p, c, grid, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_splitk_reduce(const GemmParams& p, int tt, int grid, cudaStream_t stream)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_wt * p.n_tt, tt / 16);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    switch (tt) {
+        case 16: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<16>, p, grid);
+        case 32: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<32>, p, grid);
+        case 64: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<64>, p, grid);
+        case 128: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<128>, p, grid);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -72,7 +72,7 @@ struct alignas(64) GemmParams {
     const float* as_tiles;    // [n_tt][G][TT]
     void* out;           // y bf16 [M, N] (row stride ldy), or int32 partials [G, M, N]
     float* partials;     // stream-K partial tiles: [2 * grid][TT][128] fp32
-    int* counters;       // [n_tiles] arrival counters, zero between calls
+    int* counters;       // unused (kept zero)
     int* status;         // device status word
     int M, N, Kpad, G;
     int64_t ldy;
@@ -122,5 +122,9 @@ cudaError_t launch_msd_to_kernel(const MsdToKernelParams& p, cudaStream_t stream
 cudaError_t launch_gemm(const GemmParams& p, const GemmConfig& cfg, int grid, cudaStream_t stream,
                         bool pdl);
 size_t gemm_smem_bytes(const GemmConfig& cfg);
+
+// Sums the parts of output tiles split across GEMM CTAs (a programmatic
+// dependent of the GEMM launched with the same parameters and grid).
+cudaError_t launch_splitk_reduce(const GemmParams& p, int tt, int grid, cudaStream_t stream);
 
 }  // namespace w4a8
