@@ -188,26 +188,39 @@ def l2_flush(torch, flush):
     return flush.view(torch.int64).sum()
 
 
-def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=3):
-    """GEMM-only launches on prepared weights, L2 flushed before each, CUDA
-    events on the launch stream."""
+def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=4):
+    """Per call: the GEMM (with its stream-K fix-up) on prepared weights, the L2
+    flushed by a read before each launch.  Two CUDA graphs per call -- reps x
+    [flush, GEMM] and reps x [flush] -- timed with events on the replay stream;
+    the difference is the GEMMs' time without launch gaps."""
     out = []
-    st = torch.cuda.current_stream()
     for (shape, M) in cfgs:
         packed, scale, K, N, pw = W[shape]
-        x = xs[(shape, M)]
-        ts = []
-        for _ in range(reps):
-            ops.linear_quant(x, N, GK)
-            l2_flush(torch, flush)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            ops.linear_gemm_prepared(M, pw, ys[(shape, M)])
-            e1.record(st)
-            e1.synchronize()
-            ts.append(e0.elapsed_time(e1) * 1e-3)
-        out.append((shape, M, K, N, min(ts)))
+        ops.linear_quant(xs[(shape, M)], N, GK)
+        y = ys[(shape, M)]
+        ops.linear_gemm_prepared(M, pw, y)            # workspace exists before capture
+        torch.cuda.synchronize()
+        times = []
+        for with_gemm in (True, False):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(reps):
+                    l2_flush(torch, flush)
+                    if with_gemm:
+                        ops.linear_gemm_prepared(M, pw, y)
+            g.replay()
+            torch.cuda.synchronize()
+            best = 1e9
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                e1.synchronize()
+                best = min(best, e0.elapsed_time(e1) * 1e-3)
+            times.append(best)
+            del g
+        out.append((shape, M, K, N, max(times[0] - times[1], 1e-9) / reps))
     return out
 
 
@@ -371,7 +384,8 @@ def run_gpu(args, rank, world, local_rank):
         v, dt, threads, kind, desc = cpu_sample()
         cpu = {"value": v, "unit": "GB/s", "cores": threads, "kind": kind, "sample": desc,
                "seconds": round(dt, 2)}
-    launches = 2 * len(cfgs) * args.steps
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    launches = args.steps * sum(kernels_per_call(M, W[s][3], W[s][2], sms) for (s, M) in cfgs)
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_step, "higher_is_better": True, "scaling": "weak",
@@ -385,8 +399,9 @@ def run_gpu(args, rank, world, local_rank):
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
-                     "kernel": "w4a8_gemm_kernel (GEMM alone on prepared weights, L2 flushed by a "
-                               "512 MB read before each launch)",
+                     "kernel": "w4a8_gemm_kernel + its stream-K fix-up, prepared weights, L2 flushed by a "
+                               "512 MB read before each launch; graph [flush, GEMM] minus graph [flush]",
+                     "traffic_source": "profiles/gemm_decode_traffic.json (ncu, the same 24 calls, per launch)",
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src},
         "e2e": e2e,
         "raw_layout": {"value": raw_value, "unit": "GB/s", "ms_per_step": 1e3 * t_raw,
@@ -404,6 +419,43 @@ def run_gpu(args, rank, world, local_rank):
     if tp is not None:
         line["tp_stack"] = tp
     print(json.dumps(line))
+
+
+def kernels_per_call(M, N, K, sms, gk=GK):
+    """Kernels one linear call launches: the quantiser, the GEMM and, when the
+    GEMM's stream-K split leaves a tile divided between CTAs, the fix-up kernel
+    (the host plan in csrc/w4a8_capi.cu)."""
+    tt = 16 if M <= 16 else (32 if M <= 32 else (64 if M <= 64 else 128))
+    G = -(-K // gk)
+    last = K - (G - 1) * gk
+    kpad = (G - 1) * (-(-gk // 64) * 64) + -(-last // 64) * 64
+    kb_total = -(-kpad // 256)
+    upt = -(-kb_total // (2 if tt <= 32 else 1)) if gk <= 256 else G
+    units = -(-N // 128) * -(-M // tt) * upt
+    grid = max(1, min(sms, units))
+    split = any((c * units // grid) % upt for c in range(1, grid))
+    return 3 if split else 2
+
+
+def profile_sweep():
+    """The decode sweep's 24 calls once each after a warm-up pass, L2 flushed
+    (by reading) before each: the target of the traffic capture (profiles/)."""
+    import torch
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = torch.device("cuda", 0)
+    W = build_weights(torch, dev)
+    cfgs = sweep_configs()
+    xs = {(s, M): syn.activation_torch(M, W[s][2], 100 + M, dev) for (s, M) in cfgs}
+    ys = {(s, M): torch.empty(M, W[s][3], dtype=torch.bfloat16, device=dev) for (s, M) in cfgs}
+    flush = torch.ones(512 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(2):
+        for (s, M) in cfgs:
+            l2_flush(torch, flush)
+            ops.linear_prepared(xs[(s, M)], W[s][4], out=ys[(s, M)])
+    torch.cuda.synchronize()
+    assert ops.workspace_status(dev) == 0
+    print("profile sweep: " + " ".join(f"{s}:{M}" for (s, M) in cfgs))
 
 
 def profile_case(spec: str):
@@ -437,9 +489,13 @@ def main():
     ap.add_argument("--tp-stack", action="store_true", help="also run the TP layer stack at N=1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", default=None, help="SHAPE:M, e.g. qkv:16 (ncu target)")
+    ap.add_argument("--profile-sweep", action="store_true", help="each decode call once, cold (ncu target)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args.profile_case)
+        return
+    if args.profile_sweep:
+        profile_sweep()
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

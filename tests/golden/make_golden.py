@@ -15,6 +15,8 @@ Writes ``tests/golden/golden.npz``.  Sources of truth:
   injected through ``QTensor`` exactly as the survey's config 0 describes;
 * an int64/float64 restatement of ``run_selftest._exact_reference``
   (run_selftest.py:104-121) for the int32 group partials;
+* ``npu_ops/python/w4a8_ops.quantize_weight`` (w4a8_ops.py:181-240) for the
+  asymmetric int4 weight layout (codes, bf16 scales and zero points, raw-code sums);
 * when ``oracle/_ref`` was built (``make -C oracle ref``), the reference's C++
   ``PackInt4Grouped`` / ``SplitInt8ToInt4PlanesGrouped`` /
   ``ReferenceMidGroupGemm`` for ragged-K byte layouts and bf16 outputs.
@@ -179,6 +181,29 @@ def ref_cpp_cases(out):
         out[pfx + "y"] = oracle.ref_midgroup_gemm(qa, as_bits, qw, ws_bits, wz_bits, gk)
 
 
+def weight_cases(reference, out):
+    """Weight quantiser golden: the reference's quantize_weight
+    (npu_ops/python/w4a8_ops.py:181-240) on seeded bf16 weights, including a
+    constant group, an all-positive group and a ragged last group."""
+    import torch
+    sys.path.insert(0, os.path.join(reference, "npu_ops", "python"))
+    import w4a8_ops as ref_ops
+    cases = [(256, 2048, 1024, 21), (128, 1057, 1024, 22), (128, 640, 128, 23)]
+    for i, (N, K, gk, seed) in enumerate(cases):
+        g = torch.Generator().manual_seed(seed)
+        w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+        w[0, :gk] = 0.0125                                   # constant group
+        w[1, :gk] = w[1, :gk].abs() + 0.01                   # all-positive group
+        w_q, w_scale, w_ksum, w_zero = ref_ops.quantize_weight(w, gk)
+        p = f"w{i}_"
+        out[p + "meta"] = np.array([N, K, gk], np.int64)
+        out[p + "w"] = _bits(w)
+        out[p + "wq"] = w_q.numpy()
+        out[p + "ws"] = _bits(w_scale)
+        out[p + "wk"] = w_ksum.numpy()
+        out[p + "wz"] = _bits(w_zero)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("W4A8_REFERENCE", "/root/reference"))
@@ -193,6 +218,7 @@ def main():
     quant_cases(quant, out)
     gemm_cases(quant, fl, out)
     ref_cpp_cases(out)
+    weight_cases(args.reference, out)
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {len(out)} arrays, {os.path.getsize(args.out) / 1024:.0f} KiB")
 
