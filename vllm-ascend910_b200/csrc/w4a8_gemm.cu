@@ -63,7 +63,7 @@ struct Cfg {
     static constexpr int GPU = GK <= 256 ? KS * GPK : 1;     // groups per unit (max)
     static constexpr bool SYM16 = !ASYM && GK <= 256;
     static constexpr bool MAGIC = GK <= 256;                 // magic-initialised accumulators
-    static constexpr int E = TT <= 32 ? 1 : 2;               // epilogue warpgroups
+    static constexpr int E = TT <= 16 ? 1 : 2;               // epilogue warpgroups
     static constexpr int NC = TT / E;                        // accumulator columns per thread
     static constexpr int NCH = NC / 16;                      // 16-column TMEM chunks per thread
     static constexpr int THREADS = (kNumPreWarps + 4 * E) * 32;

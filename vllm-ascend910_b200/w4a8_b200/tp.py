@@ -259,4 +259,4 @@ def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4,
                     "graph": graph is not None})
         del graph
     return {"tp": world, "layers": layers, "dims": dataclasses.asdict(d), "per_M": res,
-            "note": "attention replaced by the first hidden/tp columns of the QKV output"}
+            "note": "attention replaced by the rank's q section of the QKV output"}
