@@ -112,6 +112,13 @@ struct Cfg {
     static_assert(NC % 16 == 0, "epilogue works in 16-column chunks");
     static_assert(OFF_A % 1024 == 0 && OFF_WZ % 1024 == 0, "tile alignment");
     static_assert(SMEM <= 227 * 1024, "shared memory");
+    // Register split for the 512-thread configurations (4 warpgroups, 128
+    // registers each at launch): producers + MMA issuers, converters, and the
+    // two epilogue warpgroups that hold TT/2 fp32 accumulators per thread.
+    static constexpr bool SPLIT_REGS = THREADS == 512 && TT >= 64;
+    static constexpr int REGS_PRE = 56, REGS_CONV = 80, REGS_EPI = 184;
+    static_assert(!SPLIT_REGS || REGS_PRE + REGS_CONV + 2 * REGS_EPI <= 4 * (65536 / THREADS),
+                  "register split exceeds the launch allocation");
 };
 
 struct Bars {
@@ -332,7 +339,11 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     pdl_launch_dependents();
     const uint32_t ws_elt = ws_bf16 ? 2u : 4u;
 
+    // With SPLIT_REGS each role re-sizes its warpgroup's registers first thing
+    // in its branch (warps 0-3: producers + issuers, 4-7: converters, 8-15:
+    // epilogue), so the compiler allocates each branch for its own budget.
     if (warp == 0 || warp == kActProducerWarp) {
+        if (C::SPLIT_REGS) regs_dec<C::REGS_PRE>();
         // ============================================================ producers
         // Warp 0 streams weight tiles (and, asymmetric, the unit's zero points
         // with its first tile); it never waits for the epilogue nor for the
@@ -423,6 +434,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 mbar_wait(&bars->sfull[i % C::DS], static_cast<uint32_t>((i / C::DS) & 1), abort_flag, p.status, kWDrain);
         }
     } else if (warp <= kNumIssuers) {
+        if (C::SPLIT_REGS) regs_dec<C::REGS_PRE>();
         // ============================================================ MMA issuers
         // Issuer i owns the units u0 + i, u0 + i + 2, ...: for those it waits
         // for the stages, issues every MMA and commits the stages' buffers and
@@ -510,6 +522,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             mbar_wait(&bars->drain[me], 0, abort_flag, p.status, kWDrain);
         }
     } else if (warp < kNumPreWarps) {
+        if (C::SPLIT_REGS) regs_dec<C::REGS_CONV>();
         // ============================================================ converters
         // Unpack one weight stage into a TMEM A buffer and hand the
         // shared-memory tiles straight back to the producer.
@@ -578,6 +591,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             }
         }
     } else {
+        if (C::SPLIT_REGS) regs_inc<C::REGS_EPI>();
         // ============================================================ epilogue
         const int ew = warp - kNumPreWarps;
         const int quarter = warp & 3;
