@@ -284,7 +284,10 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
 {
     using C = Cfg<TT, GK, ASYM>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // Align by an offset from the __shared__ array itself: a pointer rebuilt from
+    // an integer loses the address space, and every read through it would be a
+    // generic load (the L1TEX path, behind the bulk copies) instead of ld.shared.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     Bars* bars = reinterpret_cast<Bars*>(smem + C::BAR_OFF);
 
     const int warp = static_cast<int>(warp_id());
