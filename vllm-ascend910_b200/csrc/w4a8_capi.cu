@@ -91,11 +91,13 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_
 struct Plan {
     int64_t M, N, K, Kpad, G;
     int gk, tt, n_wt, n_tt, upt, units, grid, kb_total;
-    size_t off_counters, off_as, off_aq, off_part, total;
+    size_t off_as, off_aq, off_part, total;
     bool split;   // some output tile's units are divided between CTAs
 };
 
-Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
+// tt_cap bounds the token tile (the debug partials mode runs 16-token tiles).
+// A smaller tile never needs more workspace than the tile chosen for M.
+Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms, int tt_cap = 128)
 {
     Plan p{};
     p.M = M;
@@ -105,6 +107,7 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
     p.G = cdiv(K, gk);
     p.Kpad = kpad_of(K, gk);
     p.tt = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
+    p.tt = std::min(p.tt, tt_cap);
     p.n_wt = static_cast<int>(cdiv(N, 128));
     p.n_tt = static_cast<int>(cdiv(M, p.tt));
     p.kb_total = static_cast<int>(cdiv(p.Kpad, 256));
@@ -117,10 +120,7 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms)
     p.split = false;
     for (int c = 1; c < p.grid && !p.split; ++c)
         p.split = (static_cast<int64_t>(c) * p.units / p.grid) % p.upt != 0;
-    size_t off = 256;                                                     // status word block
-    p.off_counters = off;
-    off += round_up(static_cast<int64_t>(p.n_wt) * p.n_tt * 4, 256);
-    off = round_up(off, 1024);
+    size_t off = 1024;                                                    // status word block
     p.off_as = off;                                                       // [n_tt][G][tt] fp32
     off += round_up(static_cast<int64_t>(p.n_tt) * p.G * p.tt * 4, 1024);
     p.off_aq = off;                                                       // [n_tt][kb_total][tt*256]
@@ -272,7 +272,6 @@ int run_gemm(const Plan& pl, const Weights& w, void* out, int64_t ldy, bool part
     g.as_tiles = reinterpret_cast<const float*>(ws + pl.off_as);
     g.out = out;
     g.partials = reinterpret_cast<float*>(ws + pl.off_part);
-    g.counters = reinterpret_cast<int*>(ws + pl.off_counters);
     g.status = reinterpret_cast<int*>(ws);
     g.M = static_cast<int>(pl.M);
     g.N = static_cast<int>(pl.N);
@@ -308,7 +307,7 @@ int check_weights(const void* w_packed, const void* w_scale, int32_t ws_dtype, c
 // One statically sized device array per device context (module data, not an
 // allocation).  Its address is looked up once per device with that device
 // current; the whole array is cleared on that first call, after which the
-// kernels leave the arrival counters and the status word at zero themselves.
+// kernels leave the status word at zero unless a wait runs out.
 __device__ __align__(256) uint8_t g_fixed_scratch[W4A8_FIXED_SCRATCH_BYTES];
 uint8_t* g_fixed_ptr[kMaxDev];
 std::mutex g_fixed_mutex;
@@ -443,7 +442,7 @@ int w4a8_group_partials(const void* x, int64_t M, int64_t K, int64_t ldx, int64_
     if (!w_packed || !aligned(w_packed, 16) || (w_zero && !aligned(w_zero, 16))) return W4A8_ERR_INVALID;
     int sms = 0;
     if ((rc = device_info(&sms)) != W4A8_OK) return rc;
-    const Plan pl = make_plan(M, N, K, gk, sms);
+    const Plan pl = make_plan(M, N, K, gk, sms, 16);
     if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -27,9 +27,9 @@
 //   * Epilogue warps: one batch of tcgen05.ld per slot, acc += P * (ws * as)
 //     with packed f32x2 arithmetic in registers, bf16 store at tile end.
 //   * Work split: stream-K over (tile, K-unit) so every SM gets the same number
-//     of weight bytes.  A tile split across CTAs is reduced deterministically
-//     by the last CTA to arrive (fixed summation order), which also resets the
-//     tile's counter for the next call.
+//     of weight bytes.  A tile split across CTAs leaves fp32 parts that a small
+//     fix-up kernel (chained by programmatic dependent launch) sums in CTA
+//     order, so the result does not depend on timing.
 //   * Every mbarrier wait is bounded (w4a8_common.cuh).
 #include "w4a8_common.cuh"
 #include "w4a8_kernels.h"
@@ -278,9 +278,12 @@ __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, 
     for (int j = 0; j < NC; ++j) __stcg(mine + (col0 + j) * 128 + row, acc_at(acc2, j));
 }
 
-template <int TT, int GK, bool ASYM>
+// PART: the debug mode that writes each group's exact int32 partials instead
+// of y.  It is a separate instantiation (16-token tiles only) so the product
+// epilogue carries no call and no second output path.
+template <int TT, int GK, bool ASYM, bool PART>
 __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
-    w4a8_gemm_kernel(const __grid_constant__ GemmParams p, const int ws_bf16, const int out_partials)
+    w4a8_gemm_kernel(const __grid_constant__ GemmParams p, const int ws_bf16)
 {
     using C = Cfg<TT, GK, ASYM>;
     extern __shared__ uint8_t smem_raw[];
@@ -361,7 +364,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 tma_prefetch_desc(&p.tm_w);
                 if (C::ASYM) tma_prefetch_desc(&p.tm_wz);
             }
-            if (!wside && !prepared && !out_partials) tma_prefetch_desc(&p.tm_ws);
+            if (!wside && !prepared && !PART) tma_prefetch_desc(&p.tm_ws);
             if (!wside) pdl_wait();
             const uint64_t pol = wside ? policy_evict_first() : policy_evict_last();
             const int ns = wside ? C::S_W : C::S_A;
@@ -377,7 +380,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 unit_groups<C>(p, un.ut, g0, g1);
                 if (!wside) {
                     if (!mbar_wait(&bars->sempty[slot], slph ^ 1, abort_flag, p.status, kWProdSlot)) break;
-                    if (out_partials) {
+                    if (PART) {
                         mbar_arrive(&bars->sfull[slot]);      // the partials mode reads no scales
                     } else {
                         const uint32_t ng = static_cast<uint32_t>(g1 - g0);
@@ -637,6 +640,17 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 if (!warp_wait(&bars->accfull[sl], aph, abort_flag, p.status, kWEpiAccFull)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t t_slot = tbase + lane_off + C::ACC0 + static_cast<uint32_t>(sl * C::CG * TT + col0);
+                // this row's weight scale of each group in the slot, read once
+                float wsv[C::CG];
+                if (!PART) {
+#pragma unroll
+                    for (int gi = 0; gi < C::CG; ++gi) {
+                        const int gl = min(gs + gi, g1 - 1) - g0;
+                        wsv[gi] = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gl * 128 + row])
+                                          : reinterpret_cast<const float*>(wsb)[gl * 128 + row];
+                        if (C::SYM16) wsv[gi] *= 0.0625f;   // the unpack carried weights as 16*w
+                    }
+                }
 #pragma unroll
                 for (int b0 = 0; b0 < C::TOTCH; b0 += C::BCH) {
                     R16 r[C::BCH];
@@ -659,14 +673,10 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         const int g = gs + gi;
                         if (g >= g1) continue;
                         const int gl = g - g0;           // group index within the unit's scale entry
-                        if (!out_partials) {
-                            float wsv = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gl * 128 + row])
-                                                : reinterpret_cast<const float*>(wsb)[gl * 128 + row];
-                            if (C::SYM16) wsv *= 0.0625f;   // the unpack carried weights as 16*w
-                            rescale_chunk<C::NC, C::MAGIC>(acc2, i, r[q], wsv, asb + gl * TT + col0 + 16 * i);
-                        } else {
+                        if (PART)
                             store_partials<C::MAGIC, C::SYM16>(p, r[q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
-                        }
+                        else
+                            rescale_chunk<C::NC, C::MAGIC>(acc2, i, r[q], wsv[gi], asb + gl * TT + col0 + 16 * i);
                     }
                 }
                 if (C::MAGIC) tc_wait_st();
@@ -684,9 +694,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
 
             // ---- end of this CTA's share of tile t: store or hand over ----
             if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
-                if (!out_partials) {
-                    flush_tile<C>(p, un, u0, u1, cta, row, col0, acc2);
-                }
+                if (!PART) flush_tile<C>(p, un, u0, u1, cta, row, col0, acc2);
 #pragma unroll
                 for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
             }
@@ -799,12 +807,11 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, 
     }
 }
 
-template <int TT, int GK, bool ASYM>
-cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pdl, int ws_bf16,
-                     int out_partials)
+template <int TT, int GK, bool ASYM, bool PART>
+cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pdl, int ws_bf16)
 {
     using C = Cfg<TT, GK, ASYM>;
-    auto kern = w4a8_gemm_kernel<TT, GK, ASYM>;
+    auto kern = w4a8_gemm_kernel<TT, GK, ASYM, PART>;
     // The shared-memory opt-in is per device; set it once per device.
     static bool attr_done[64] = {};
     int dev = 0;
@@ -825,14 +832,22 @@ cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pd
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, p, ws_bf16, out_partials);
+    return cudaLaunchKernelEx(&cfg, kern, p, ws_bf16);
 }
 
 template <int TT, int GK>
 cudaError_t launch_gk(const GemmParams& p, const GemmConfig& c, int grid, cudaStream_t s, bool pdl)
 {
-    return c.asym ? launch_t<TT, GK, true>(p, grid, s, pdl, c.ws_bf16, c.partials)
-                  : launch_t<TT, GK, false>(p, grid, s, pdl, c.ws_bf16, c.partials);
+    if (c.partials) {
+        // the debug partials mode exists for 16-token tiles only (the host plans it so)
+        if constexpr (TT == 16)
+            return c.asym ? launch_t<TT, GK, true, true>(p, grid, s, pdl, c.ws_bf16)
+                          : launch_t<TT, GK, false, true>(p, grid, s, pdl, c.ws_bf16);
+        else
+            return cudaErrorInvalidValue;
+    }
+    return c.asym ? launch_t<TT, GK, true, false>(p, grid, s, pdl, c.ws_bf16)
+                  : launch_t<TT, GK, false, false>(p, grid, s, pdl, c.ws_bf16);
 }
 
 template <int TT>

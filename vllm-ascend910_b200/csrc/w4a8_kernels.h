@@ -72,7 +72,6 @@ struct alignas(64) GemmParams {
     const float* as_tiles;    // [n_tt][G][TT]
     void* out;           // y bf16 [M, N] (row stride ldy), or int32 partials [G, M, N]
     float* partials;     // stream-K partial tiles: [2 * grid][TT][128] fp32
-    int* counters;       // unused (kept zero)
     int* status;         // device status word
     int M, N, Kpad, G;
     int64_t ldy;
