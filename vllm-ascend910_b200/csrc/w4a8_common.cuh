@@ -21,13 +21,6 @@ enum : int {
     kDevTimeoutBase = 0x100,   // + role/wait id
 };
 
-// fp32 whose bit pattern is 0x4B400000: 1.5 * 2^23.  An int32 accumulator
-// initialised to these bits and advanced by an integer P (|P| <= 2^22) holds
-// the float (1.5 * 2^23 + P) exactly, so float(P) = bits_as_float - kMagicF
-// with one exact subtraction.
-constexpr uint32_t kMagicBits = 0x4B400000u;
-constexpr float kMagicF = 12582912.0f;
-
 // Wall-clock limit for any single wait (nanoseconds of %globaltimer).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
 
@@ -248,16 +241,6 @@ __device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8])
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-        : "memory");
-}
-
-// 16 columns of one repeated value.
-__device__ __forceinline__ void tc_st16_fill(uint32_t taddr, uint32_t v)
-{
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 "
-        "[%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-        "r"(v)
         : "memory");
 }
 

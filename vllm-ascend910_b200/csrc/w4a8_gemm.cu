@@ -22,8 +22,7 @@
 //     handed to the epilogue through a ring of up to 8 accumulator slots (a
 //     slot holds one K-unit's groups when the token tile is small, else one
 //     group), so the MMA runs several groups ahead of the rescale instead of
-//     waiting for it.  For GK <= 256 a region is pre-set to the bits of
-//     1.5*2^23, so float(P) is one exact fp32 subtraction in the epilogue.
+//     waiting for it.  A group's first MMA overwrites its region (no clear).
 //   * Epilogue warps: one batch of tcgen05.ld per slot, acc += P * (ws * as)
 //     with packed f32x2 arithmetic in registers, bf16 store at tile end.
 //   * Work split: stream-K over (tile, K-unit) so every SM gets the same number
@@ -62,7 +61,6 @@ struct Cfg {
     static constexpr int UKB = GK <= 256 ? KS : GK / 256;    // k-blocks per unit (max)
     static constexpr int GPU = GK <= 256 ? KS * GPK : 1;     // groups per unit (max)
     static constexpr bool SYM16 = !ASYM && GK <= 256;
-    static constexpr bool MAGIC = GK <= 256;                 // magic-initialised accumulators
     static constexpr int E = TT <= 16 ? 1 : 2;               // epilogue warpgroups
     static constexpr int NC = TT / E;                        // accumulator columns per thread
     static constexpr int NCH = NC / 16;                      // 16-column TMEM chunks per thread
@@ -198,34 +196,26 @@ __device__ __forceinline__ int cta_of_unit(const GemmParams& p, int u, int C)
     return static_cast<int>((static_cast<int64_t>(u + 1) * C - 1) / p.total_units);
 }
 
-// acc[j] += float(P_j) * (ws * as[j]) for NC consecutive columns, in packed
-// f32x2 arithmetic.  r holds the accumulator bits: 1.5*2^23 + P (MAGIC) or P.
 struct R16 {
     uint32_t v[16];
 };
 
 // acc[16*i + j] += float(P_j) * (ws * as[j]) for one 16-column chunk.  The
-// accumulator lives in packed fp32 pairs (acc2[k] = columns 2k, 2k+1) so each
-// step is one f32x2 instruction on a register pair.  r holds the accumulator
-// bits: 1.5*2^23 + P (MAGIC) or P.
-template <int NC, bool MAGIC>
+// accumulator lives in packed fp32 pairs (acc2[k] = columns 2k, 2k+1) so the
+// scale and accumulate steps are f32x2 instructions on register pairs.  r holds
+// the int32 group partials P (|P| < 2^23, so the conversion is exact).
+template <int NC>
 __device__ __forceinline__ void rescale_chunk(uint64_t (&acc2)[NC / 2], int i, const R16& r, float wsv,
                                               const float* asg)
 {
     const uint64_t ws2 = pack2(wsv, wsv);
-    const uint64_t mg2 = pack2(kMagicF, kMagicF);
 #pragma unroll
     for (int j = 0; j < 16; j += 4) {
         const float4 a4 = *reinterpret_cast<const float4*>(asg + j);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const uint32_t r0 = r.v[j + 2 * h], r1 = r.v[j + 2 * h + 1];
-            uint64_t f2;
-            if (MAGIC) {
-                f2 = f2_sub(pack2u(r0, r1), mg2);
-            } else {
-                f2 = pack2(static_cast<float>(static_cast<int>(r0)), static_cast<float>(static_cast<int>(r1)));
-            }
+            const uint64_t f2 = pack2(__int2float_rn(static_cast<int>(r0)), __int2float_rn(static_cast<int>(r1)));
             const uint64_t c2 = f2_mul(ws2, h == 0 ? pack2(a4.x, a4.y) : pack2(a4.z, a4.w));
             uint64_t& a = acc2[8 * i + j / 2 + h];
             a = f2_fma(f2, c2, a);
@@ -239,14 +229,14 @@ __device__ __forceinline__ float acc_at(const uint64_t* acc2, int j)
 }
 
 // Debug output mode: the exact int32 partials of one 16-column chunk of group g.
-template <bool MAGIC, bool SYM16>
+template <bool SYM16>
 __device__ __noinline__ void store_partials(const GemmParams& p, R16 r, int g, int m0, int n)
 {
     if (n >= p.N) return;
     int* dst = reinterpret_cast<int*>(p.out) + (static_cast<int64_t>(g) * p.M + m0) * p.N + n;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        int P = MAGIC ? static_cast<int>(r.v[j] - kMagicBits) : static_cast<int>(r.v[j]);
+        int P = static_cast<int>(r.v[j]);
         if (SYM16) P >>= 4;
         if (m0 + j < p.M) dst[static_cast<int64_t>(j) * p.N] = P;
     }
@@ -482,7 +472,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                                 for (int t = 0; t < C::GK / 32; ++t) {
                                     const int ks = s0 + t;
                                     const uint64_t bd = smem_desc_sw128(a_smem + j * C::A_TILE + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
-                                    tc_mma_i8_ts(d_tmem, a_tmem + j * 64 + ks * 8, bd, idesc, 1u);
+                                    tc_mma_i8_ts(d_tmem, a_tmem + j * 64 + ks * 8, bd, idesc, t == 0 ? 0u : 1u);
                                 }
                                 if (gi == C::CG - 1 || g == g1 - 1) {
                                     tc_commit(&bars->accfull[sl]);
@@ -607,15 +597,6 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         constexpr int NCH = C::NCH;
 
-        if (C::MAGIC) {
-            for (int b = 0; b < C::NACC; ++b)
-#pragma unroll
-                for (int gi = 0; gi < C::CG; ++gi)
-#pragma unroll
-                    for (int i = 0; i < NCH; ++i)
-                        tc_st16_fill(tbase + lane_off + C::ACC0 + (b * C::CG + gi) * TT + col0 + 16 * i, kMagicBits);
-            tc_wait_st();
-        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0)
@@ -660,13 +641,6 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         tc_ld16(t_slot + (c / NCH) * TT + 16 * (c % NCH), r[q].v);
                     }
                     tc_wait_ld();
-                    if (C::MAGIC) {
-#pragma unroll
-                        for (int q = 0; q < C::BCH; ++q) {
-                            const int c = b0 + q;
-                            tc_st16_fill(t_slot + (c / NCH) * TT + 16 * (c % NCH), kMagicBits);
-                        }
-                    }
 #pragma unroll
                     for (int q = 0; q < C::BCH; ++q) {
                         const int c = b0 + q, gi = c / NCH, i = c % NCH;
@@ -674,12 +648,11 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         if (g >= g1) continue;
                         const int gl = g - g0;           // group index within the unit's scale entry
                         if (PART)
-                            store_partials<C::MAGIC, C::SYM16>(p, r[q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
+                            store_partials<C::SYM16>(p, r[q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
                         else
-                            rescale_chunk<C::NC, C::MAGIC>(acc2, i, r[q], wsv[gi], asb + gl * TT + col0 + 16 * i);
+                            rescale_chunk<C::NC>(acc2, i, r[q], wsv[gi], asb + gl * TT + col0 + 16 * i);
                     }
                 }
-                if (C::MAGIC) tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->accempty[sl]);
