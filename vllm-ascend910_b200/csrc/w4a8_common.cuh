@@ -236,6 +236,16 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16])
         : "r"(taddr));
 }
 
+// Orders later uses of tcgen05.ld destination registers after the
+// tcgen05.wait::ld that precedes this call: the empty volatile asm is not moved
+// across the wait, and every later read of r depends on its outputs.
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16])
+{
+    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                 "+r"(r[14]), "+r"(r[15]));
+}
+
 __device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8])
 {
     asm volatile(

@@ -75,6 +75,10 @@ struct Cfg {
     static constexpr int CG = GPU <= CG_FIT ? GPU : (CG_FIT >= 4 ? 4 : (CG_FIT >= 2 ? 2 : 1));
     static constexpr int TOTCH = CG * NCH;                   // 16-column chunks per slot and thread
     static constexpr int BCH = TOTCH < 2 ? TOTCH : 2;        // chunks per tcgen05.ld batch
+    static constexpr int NB = TOTCH / BCH;                   // batches per slot
+    // Releasing a slot before its rescale (measured): faster for 32-token
+    // tiles, slower for 128-token tiles, neutral otherwise.
+    static constexpr bool EARLY_RELEASE = TT == 32;
     static constexpr int NACC_FIT = ACC_COLS / (CG * TT);
     static constexpr int NACC = NACC_FIT > 8 ? 8 : NACC_FIT;           // accumulator slots
     __host__ __device__ static constexpr int r128(int x) { return (x + 127) / 128 * 128; }
@@ -108,14 +112,22 @@ struct Cfg {
     static_assert(NACC >= 2, "need at least two accumulator slots");
     static_assert(GPU % CG == 0, "slots split a unit evenly");
     static_assert(NC % 16 == 0, "epilogue works in 16-column chunks");
+    static_assert(TOTCH % BCH == 0, "slots split into whole batches");
     static_assert(OFF_A % 1024 == 0 && OFF_WZ % 1024 == 0, "tile alignment");
     static_assert(SMEM <= 227 * 1024, "shared memory");
-    // Register split for the 512-thread configurations (4 warpgroups, 128
-    // registers each at launch): producers + MMA issuers, converters, and the
-    // two epilogue warpgroups that hold TT/2 fp32 accumulators per thread.
-    static constexpr bool SPLIT_REGS = THREADS == 512 && TT >= 64;
-    static constexpr int REGS_PRE = 56, REGS_CONV = 80, REGS_EPI = 184;
-    static_assert(!SPLIT_REGS || REGS_PRE + REGS_CONV + 2 * REGS_EPI <= 4 * (65536 / THREADS),
+    // Register split for the 64/128-token tiles (2 + E warpgroups): producers +
+    // MMA issuers and converters give registers to the epilogue warpgroups,
+    // which hold NC fp32 accumulators per thread.  The sum stays within the
+    // launch allocation (__launch_bounds__(THREADS, 1): LAUNCH_REGS per thread);
+    // the host also checks it against the compiled register count.
+    static constexpr int NWG = 2 + E;
+    static constexpr bool SPLIT_REGS = TT >= 64;
+    static constexpr int LAUNCH_REGS = (65536 / THREADS) / 8 * 8;
+    static constexpr int REGS_PRE = 56;
+    static constexpr int REGS_CONV = E <= 2 ? 80 : 72;
+    static constexpr int REGS_EPI = ((NWG * LAUNCH_REGS - REGS_PRE - REGS_CONV) / E) / 8 * 8;
+    static constexpr int REG_SUM = REGS_PRE + REGS_CONV + E * REGS_EPI;
+    static_assert(!SPLIT_REGS || (REG_SUM <= NWG * LAUNCH_REGS && REGS_EPI <= 256 && REGS_EPI >= REGS_CONV),
                   "register split exceeds the launch allocation");
 };
 
@@ -632,31 +644,54 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         if (C::SYM16) wsv[gi] *= 0.0625f;   // the unpack carried weights as 16*w
                     }
                 }
+                // Batches of BCH chunks, software-pipelined: the next batch's
+                // tcgen05.ld is in flight while this batch is rescaled.  With
+                // EARLY_RELEASE the slot goes back to the MMA as soon as its last
+                // batch is in registers, otherwise after the rescale.
+                R16 r[2][C::BCH];
 #pragma unroll
-                for (int b0 = 0; b0 < C::TOTCH; b0 += C::BCH) {
-                    R16 r[C::BCH];
+                for (int q = 0; q < C::BCH; ++q)
+                    tc_ld16(t_slot + (q / NCH) * TT + 16 * (q % NCH), r[0][q].v);
+                tc_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < C::BCH; ++q) {
-                        const int c = b0 + q;
-                        tc_ld16(t_slot + (c / NCH) * TT + 16 * (c % NCH), r[q].v);
+                for (int q = 0; q < C::BCH; ++q) reg_fence16(r[0][q].v);
+#pragma unroll
+                for (int b = 0; b < C::NB; ++b) {
+                    if (b + 1 < C::NB) {
+#pragma unroll
+                        for (int q = 0; q < C::BCH; ++q) {
+                            const int c = (b + 1) * C::BCH + q;
+                            tc_ld16(t_slot + (c / NCH) * TT + 16 * (c % NCH), r[(b + 1) & 1][q].v);
+                        }
+                    } else if (C::EARLY_RELEASE) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bars->accempty[sl]);
+                        __syncwarp();
                     }
-                    tc_wait_ld();
 #pragma unroll
                     for (int q = 0; q < C::BCH; ++q) {
-                        const int c = b0 + q, gi = c / NCH, i = c % NCH;
+                        const int c = b * C::BCH + q, gi = c / NCH, i = c % NCH;
                         const int g = gs + gi;
                         if (g >= g1) continue;
                         const int gl = g - g0;           // group index within the unit's scale entry
                         if (PART)
-                            store_partials<C::SYM16>(p, r[q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
+                            store_partials<C::SYM16>(p, r[b & 1][q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
                         else
-                            rescale_chunk<C::NC>(acc2, i, r[q], wsv[gi], asb + gl * TT + col0 + 16 * i);
+                            rescale_chunk<C::NC>(acc2, i, r[b & 1][q], wsv[gi], asb + gl * TT + col0 + 16 * i);
+                    }
+                    if (b + 1 < C::NB) {
+                        tc_wait_ld();
+#pragma unroll
+                        for (int q = 0; q < C::BCH; ++q) reg_fence16(r[(b + 1) & 1][q].v);
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->accempty[sl]);
-                __syncwarp();
+                if (!C::EARLY_RELEASE) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->accempty[sl]);
+                    __syncwarp();
+                }
                 if (++sl == C::NACC) { sl = 0; aph ^= 1; }
             }
             if (!ok) break;
@@ -793,6 +828,15 @@ cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pd
     if (dev < 0 || dev >= 64 || !attr_done[dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
+        if (C::SPLIT_REGS) {
+            // setmaxnreg.inc waits for registers the other warpgroups released:
+            // refuse a build whose launch allocation cannot cover the split.
+            cudaFuncAttributes fa{};
+            e = cudaFuncGetAttributes(&fa, kern);
+            if (e != cudaSuccess) return e;
+            if (static_cast<int64_t>(fa.numRegs) * C::THREADS < static_cast<int64_t>(C::REG_SUM) * 128)
+                return cudaErrorInvalidConfiguration;
+        }
         if (dev >= 0 && dev < 64) attr_done[dev] = true;
     }
     cudaLaunchConfig_t cfg = {};
