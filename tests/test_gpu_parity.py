@@ -177,6 +177,34 @@ def test_linear_tolerance(orc, M, N, K, gk, asym, sd):
     assert ops.workspace_status() == 0
 
 
+# Shapes where every CTA runs four or more K-units, so the accumulator-slot
+# ring wraps many times and both MMA issuers run ahead of the epilogue (with
+# GK = 64 a unit fills 4 slots, as many as or more than the ring holds).
+MANY_UNIT_CASES = [  # M, N, K, gk, asym, scale_dtype
+    (130, 2048, 5120, 64, False, "f32"), (64, 4096, 5120, 64, True, "bf16"), (32, 8192, 5120, 64, False, "f32"),
+    (16, 8192, 5120, 64, False, "bf16"), (256, 2048, 5120, 128, False, "f32"), (100, 2048, 5120, 256, True, "f32"),
+]
+
+
+@pytest.mark.parametrize("M,N,K,gk,asym,sd", MANY_UNIT_CASES)
+def test_linear_many_units_per_cta(orc, M, N, K, gk, asym, sd):
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    xb = syn.activation_np(M, K, 7000 + M + gk)
+    w = syn.weight_np(N, K, gk, 8000 + N + gk, asym=asym, scale_bf16=(sd == "bf16"))
+    packed, ws, wz = _weights(w, gk, dev, torch.bfloat16 if sd == "bf16" else torch.float32)
+    x = _bf16_cuda(xb)
+    y = ops.linear(x, packed, ws, wz, gk)
+    assert ops.workspace_status() == 0
+    y64, _ = orc.linear(xb, w.codes, w.scale, w.zero, gk, exact=True)
+    _close(orc.bf16_to_f32(_bits(y)), y64)
+    # repeated calls give the same bits (no dependence on timing)
+    for _ in range(3):
+        assert np.array_equal(_bits(ops.linear(x, packed, ws, wz, gk)), _bits(y))
+    assert ops.workspace_status() == 0
+
+
 @pytest.mark.parametrize("M,N,K,gk,asym,sd", LINEAR_CASES)
 def test_linear_prepared_matches_raw(orc, M, N, K, gk, asym, sd):
     """Prepared (tile-order) weights give the same bits as the reference layout."""

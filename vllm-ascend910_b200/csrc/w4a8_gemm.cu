@@ -516,10 +516,19 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         tc_commit(&bars->tempty[ab]);
                         tc_commit(&bars->aempty[sa]);
                     } else {
-                        // the other issuer's stage: keep the slot position in step
+                        // The other issuer's stage: wait on its slots' phases as
+                        // well.  mbarrier waits match a phase by parity only, so
+                        // an issuer that skipped the other's phases could take a
+                        // phase from two rounds back for its own whenever a unit
+                        // uses as many slots as the ring holds.  The epilogue frees
+                        // slots in order, so these waits never hold the issuer
+                        // longer than its own next wait would.
                         const int nslots = C::GK <= 256 ? (g1 - g0 + C::CG - 1) / C::CG : (kbs + kn >= kb1 ? 1 : 0);
-                        for (int i = 0; i < nslots; ++i)
+                        for (int i = 0; i < nslots; ++i) {
+                            if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                             if (++sl == C::NACC) { sl = 0; slph ^= 1; }
+                        }
+                        if (!ok) break;
                     }
                     if (++ab == C::NA) { ab = 0; abph ^= 1; }
                     if (++sa == C::S_A) { sa = 0; saph ^= 1; }
