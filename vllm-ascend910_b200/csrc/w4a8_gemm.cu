@@ -368,7 +368,10 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             }
             if (!wside && !prepared && !PART) tma_prefetch_desc(&p.tm_ws);
             if (!wside) pdl_wait();
-            const uint64_t pol = wside ? policy_evict_first() : policy_evict_last();
+            // Weights stream once when there is one token tile (decode): evict
+            // them first.  With several token tiles a CTA re-reads its weight
+            // tile once per token tile, so they must stay in L2.
+            const uint64_t pol = (wside && p.n_tt == 1) ? policy_evict_first() : policy_evict_last();
             const int ns = wside ? C::S_W : C::S_A;
             uint64_t* fullb = wside ? bars->wfull : bars->afull;
             uint64_t* emptyb = wside ? bars->wempty : bars->aempty;
