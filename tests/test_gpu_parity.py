@@ -177,6 +177,38 @@ def test_linear_tolerance(orc, M, N, K, gk, asym, sd):
     assert ops.workspace_status() == 0
 
 
+def test_negative_controls_cuda(orc):
+    """Negative controls on the CUDA path, each of which must fail parity.
+
+    (a) a_ksum: the quantiser's negated group sums carry the zero-point term of
+    the reference's kernel form, P = A_q.W_q + a_ksum * wz (fake_linear.py:170-178).
+    With the GPU quantiser's a_ksum the tensor-core partials of asymmetric weights
+    come out exactly; with its sign flipped they do not.
+    (b) asymmetric weights run on the symmetric path (zero points dropped) must
+    not meet the tolerance against the asymmetric reference, while matching the
+    reference evaluated the same way (the kernel computed what it was given)."""
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    dev = _dev()
+    M, N, K, gk = 16, 256, 1280, 128
+    xb = syn.activation_np(M, K, 9100)
+    w = syn.weight_np(N, K, gk, 9200, asym=True)
+    packed, ws, wz = _weights(w, gk, dev)
+    x = _bf16_cuda(xb)
+    _, _, ks = ops.quant_act(x, gk)
+    P_aw = ops.group_partials(x, packed, None, gk).cpu().numpy().astype(np.int64)
+    P = ops.group_partials(x, packed, wz, gk).cpu().numpy().astype(np.int64)
+    term = ks.cpu().numpy().astype(np.int64)[:, :, None] * w.zero.astype(np.int64)[:, None, :]
+    assert np.array_equal(P_aw + term, P)
+    assert not np.array_equal(P_aw - term, P)
+    y_sym = orc.bf16_to_f32(_bits(ops.linear(x, packed, ws, None, gk))).astype(np.float64)
+    y_asym64, _ = orc.linear(xb, w.codes, w.scale, w.zero, gk, exact=True)
+    assert np.abs(y_sym - y_asym64).max() / np.abs(y_asym64).max() > 1e-2
+    y_sym64, _ = orc.linear(xb, w.codes, w.scale, None, gk, exact=True)
+    _close(y_sym, y_sym64)
+    assert ops.workspace_status() == 0
+
+
 # Shapes where every CTA runs four or more K-units, so the accumulator-slot
 # ring wraps many times and both MMA issuers run ahead of the epilogue (with
 # GK = 64 a unit fills 4 slots, as many as or more than the ring holds).

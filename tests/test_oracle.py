@@ -105,6 +105,36 @@ def test_ragged_layout_gate(orc):
     assert out.returncode == 0 and "ALL PASS" in out.stdout
 
 
+def test_negative_control_flipped_a_ksum_fails(golden, orc):
+    """The quantiser's negated group sums a_ksum carry the zero-point term of the
+    reference's kernel form, P = A_q.W_q + a_ksum * wz (fake_linear.py:170-178):
+    with the quantiser's a_ksum the golden partials come out exactly, with its
+    sign flipped they do not."""
+    p = "g2_"
+    M, N, K, gk, asym, _ = (int(v) for v in golden[p + "meta"])
+    assert asym
+    q, s, ks = orc.quant_act(golden[p + "x"], gk)               # ks: int32 [G, M]
+    P_aw = orc.group_partials(q, golden[p + "codes"], None, gk).astype(np.int64)   # sum A_q * W_q
+    wz = golden[p + "wz"].astype(np.int64)                        # [G, N], integers
+    good = P_aw + ks.astype(np.int64)[:, :, None] * wz[:, None, :]
+    bad = P_aw - ks.astype(np.int64)[:, :, None] * wz[:, None, :]
+    assert np.array_equal(good, golden[p + "P"])
+    assert not np.array_equal(bad, golden[p + "P"])
+
+
+def test_negative_control_asym_data_on_sym_path_fails(golden, orc):
+    """Asymmetric weights run as if symmetric (zero points dropped) must not
+    reproduce the asymmetric reference: partials or y."""
+    p = "g2_"
+    M, N, K, gk, asym, _ = (int(v) for v in golden[p + "meta"])
+    q, s, ks = orc.quant_act(golden[p + "x"], gk)
+    P_sym = orc.group_partials(q, golden[p + "codes"], None, gk)
+    assert not np.array_equal(P_sym, golden[p + "P"])
+    y_sym, _ = orc.linear(golden[p + "x"], golden[p + "codes"], golden[p + "ws"], None, gk, exact=True)
+    ref = golden[p + "y64"]
+    assert np.abs(y_sym - ref).max() / np.abs(ref).max() > 1e-2
+
+
 def test_negative_control_flipped_ksum_fails(golden, orc):
     """A planted mistake in the oracle (flipped zero-point sign) must break parity."""
     p = "g2_"
