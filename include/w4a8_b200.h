@@ -42,6 +42,7 @@ extern "C" {
 #define W4A8_ERR_CUDA (-3)        /* a CUDA call failed: w4a8_last_cuda_error()  */
 #define W4A8_ERR_WORKSPACE (-4)   /* workspace missing or smaller than required  */
 #define W4A8_ERR_DEVICE (-5)      /* current device is not an sm_100 part         */
+#define W4A8_ERR_TIMEOUT (-6)     /* a device-side wait on a peer ran out          */
 
 #define W4A8_DTYPE_BF16 0
 #define W4A8_DTYPE_F32 1
@@ -161,6 +162,35 @@ W4A8_API int w4a8_midgroup_w4a8_gemm(const int8_t* a_hi, const int8_t* a_lo, con
 W4A8_API int w4a8_group_partials(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N,
                         int32_t group_size, const void* w_packed, const void* w_zero,
                         int32_t* partials, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- one-shot all-reduce over peer memory (tensor-parallel row reductions) ----
+ * Replaces the reference's peer-read all-reduce (npu_ops/kernel/peer_allreduce_f32.cpp:127-270,
+ * driven from npu_ops/python/peer_allreduce.py) for small bf16 messages.  One
+ * handle per rank and device; every rank of the group calls
+ * w4a8_ar_allreduce_bf16 in the same order with the same count.
+ *   create:     allocates one buffer of two message slots of max_bytes plus flags
+ *               (max_bytes a multiple of 16); world <= 8.
+ *   ipc_handle: this rank's CUDA IPC handle (w4a8_ar_ipc_handle_size() bytes);
+ *   open_peers: `handles` = world handles concatenated in rank order (own ignored).
+ *   allreduce:  out[i] = bf16(sum over ranks, in rank order, of in[i] in fp32);
+ *               count a multiple of 8 elements, count * 2 <= max_bytes, in / out
+ *               16-byte aligned, in == out allowed.  Graph-capturable.  A wait for
+ *               a peer is bounded (1 s): on expiry the call leaves its output
+ *               untouched and records the failure, which w4a8_ar_status returns
+ *               as W4A8_ERR_TIMEOUT (after the stream's work is done).
+ * This entry point allocates device memory in create (nothing at call time). */
+typedef struct w4a8_ar w4a8_ar;
+W4A8_API size_t w4a8_ar_ipc_handle_size(void);
+W4A8_API int w4a8_ar_create(int32_t rank, int32_t world, size_t max_bytes, w4a8_ar** out);
+W4A8_API int w4a8_ar_ipc_handle(w4a8_ar* h, void* handle_out);
+W4A8_API int w4a8_ar_open_peers(w4a8_ar* h, const void* handles);
+/* Same, for ranks driven from this process (peers[r] = rank r's handle, own
+ * ignored; on other devices peer access is enabled). */
+W4A8_API int w4a8_ar_open_local(w4a8_ar* h, w4a8_ar* const* peers);
+W4A8_API size_t w4a8_ar_max_bytes(const w4a8_ar* h);
+W4A8_API int w4a8_ar_allreduce_bf16(w4a8_ar* h, const void* in, void* out, int64_t count, void* stream);
+W4A8_API int w4a8_ar_status(w4a8_ar* h, int32_t reset);
+W4A8_API int w4a8_ar_destroy(w4a8_ar* h);
 
 /* ---- status ---- */
 /* Synchronises `stream` and returns the device status word of `workspace`

@@ -1,0 +1,101 @@
+"""The one-shot custom all-reduce: single-GPU checks here, two-GPU runs in
+child processes (skipped with fewer than two GPUs)."""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def test_world1_is_a_copy():
+    from w4a8_b200.allreduce import _Handle
+    dev = _dev()
+    h = _Handle(0, 1, 1 << 16)
+    try:
+        h.open_local([h])
+        x = torch.randn(5120, device=dev).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        h.allreduce(x, y)
+        torch.cuda.synchronize()
+        assert torch.equal(x, y) and h.status() == 0
+        with pytest.raises(RuntimeError):          # count * 2 > max_bytes
+            h.allreduce(torch.empty(1 << 16, dtype=torch.bfloat16, device=dev),
+                        torch.empty(1 << 16, dtype=torch.bfloat16, device=dev))
+    finally:
+        h.destroy()
+
+
+def test_absent_peer_times_out_and_leaves_output():
+    """Rank 1's handle exists but its kernel never runs: rank 0's wait on a flag
+    nothing sets must run out (1 s), be reported, and leave the output alone."""
+    from w4a8_b200 import _lib
+    from w4a8_b200.allreduce import _Handle
+    dev = _dev()
+    h0, h1 = _Handle(0, 2, 1 << 16), _Handle(1, 2, 1 << 16)
+    try:
+        h0.open_local([h0, h1])
+        x = torch.randn(4096, device=dev).to(torch.bfloat16)
+        y = torch.full_like(x, 7.0)
+        h0.allreduce(x, y)
+        torch.cuda.synchronize()
+        assert h0.status(reset=True) == _lib.ERR_TIMEOUT
+        assert torch.all(y == 7.0)
+        assert h0.status() == 0                    # reset
+    finally:
+        torch.cuda.synchronize()
+        h0.destroy()
+        h1.destroy()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run_two(mode, tmp_path, timeout=240):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    port = str(_free_port())
+    procs, outs = [], []
+    for r in range(2):
+        out = str(tmp_path / f"ar_{mode}_{r}.json")
+        outs.append(out)
+        procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "ar_worker.py"), str(r), "2", port, mode, out],
+                                      env=dict(os.environ), start_new_session=True))
+    try:
+        for p in procs:
+            p.wait(timeout=timeout)
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                os.killpg(p.pid, 9)
+    return [json.load(open(o)) for o in outs]
+
+
+def test_two_gpus_parity_graph_and_fallback(tmp_path):
+    vs = _run_two("parity", tmp_path)
+    for v in vs:
+        assert v["ok"], v
+        assert v["calls_custom"] >= 6 and v["calls_fallback"] == 1
+    print({k: v for k, v in vs[0].items() if k.startswith("us_")})
+
+
+def test_two_gpus_absent_rank(tmp_path):
+    vs = _run_two("absent", tmp_path)
+    assert vs[0]["ok"] and any("timed out" in m for m in vs[0]["msgs"]), vs[0]
+    assert vs[1]["ok"], vs[1]

@@ -642,6 +642,7 @@ const char* w4a8_status_string(int s)
         case W4A8_ERR_CUDA: return "CUDA call failed (see w4a8_last_cuda_error)";
         case W4A8_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
         case W4A8_ERR_DEVICE: return "current device is not an sm_100 GPU";
+        case W4A8_ERR_TIMEOUT: return "a device-side wait on a peer rank timed out";
         default: return s >= 0x100 ? "a kernel pipeline wait timed out" : "unknown status";
     }
 }

@@ -18,6 +18,7 @@ ERR_UNSUPPORTED = -2
 ERR_CUDA = -3
 ERR_WORKSPACE = -4
 ERR_DEVICE = -5
+ERR_TIMEOUT = -6
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
 FIXED_SCRATCH_BYTES = 16 << 20   # W4A8_FIXED_SCRATCH_BYTES
@@ -55,6 +56,15 @@ SIGNATURES = [
      [_p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64, _i64, _i32, _p, _p, _sz, _p]),
     ("w4a8_group_partials", ctypes.c_int,
      [_p, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _sz, _p]),
+    ("w4a8_ar_ipc_handle_size", _sz, []),
+    ("w4a8_ar_create", ctypes.c_int, [_i32, _i32, _sz, ctypes.POINTER(_p)]),
+    ("w4a8_ar_ipc_handle", ctypes.c_int, [_p, _p]),
+    ("w4a8_ar_open_peers", ctypes.c_int, [_p, _p]),
+    ("w4a8_ar_open_local", ctypes.c_int, [_p, _p]),
+    ("w4a8_ar_max_bytes", _sz, [_p]),
+    ("w4a8_ar_allreduce_bf16", ctypes.c_int, [_p, _p, _p, _i64, _p]),
+    ("w4a8_ar_status", ctypes.c_int, [_p, _i32]),
+    ("w4a8_ar_destroy", ctypes.c_int, [_p]),
     ("w4a8_workspace_status", ctypes.c_int, [_p, _i32, _p]),
     ("w4a8_status_string", ctypes.c_char_p, [ctypes.c_int]),
     ("w4a8_last_cuda_error", ctypes.c_int, []),

@@ -207,17 +207,48 @@ def _roofline_seconds(layers: Sequence[LayerShard], M: int, hbm_gbs: float, i8_t
     return t
 
 
+def custom_allreduce(group=None, max_bytes: Optional[int] = None):
+    """The one-shot peer-memory all-reduce (``allreduce.CustomAllReduce``) for
+    messages up to ``max_bytes`` (default: M = 64 rows of hidden 5120), NCCL
+    beyond."""
+    from .allreduce import DEFAULT_MAX_BYTES, CustomAllReduce
+    return CustomAllReduce(group=group, max_bytes=max_bytes or DEFAULT_MAX_BYTES)
+
+
 def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4, iters: int = 10,
-                hbm_gbs: float = 6556.5, i8_tops: Optional[float] = None) -> Dict:
+                hbm_gbs: float = 6556.5, i8_tops: Optional[float] = None,
+                allreduces: Sequence[str] = ("nccl",)) -> Dict:
     """Time `layers` sharded layers at each M on `world` GPUs (one rank each).
 
-    The step is captured in a CUDA graph (NCCL included); the time is the max
-    over ranks of CUDA-event time per forward.  Returns tokens/s (M per forward)
-    and layer-tokens/s (M x layers per forward) with the roofline fraction."""
-    import torch.distributed as dist
+    The step is captured in a CUDA graph (the all-reduces included); the time is
+    the max over ranks of CUDA-event time per forward.  Returns tokens/s (M per
+    forward) and layer-tokens/s (M x layers per forward) with the roofline
+    fraction, per all-reduce (``nccl``, or ``custom``: the one-shot kernel for
+    small messages, NCCL for the rest)."""
     d = QWQ
     Ls = build_layers(layers, rank, world, dev, d, prepare=True)
-    ar = nccl_allreduce() if world > 1 else (lambda t: None)
+    out = {"tp": world, "layers": layers, "dims": dataclasses.asdict(d),
+           "note": "attention replaced by the rank's q section of the QKV output"}
+    for mode in allreduces:
+        car = None
+        if world == 1:
+            ar = (lambda t: None)
+        elif mode == "custom":
+            car = custom_allreduce()
+            ar = car
+        else:
+            ar = nccl_allreduce()
+        key = "per_M" if mode == "nccl" else f"per_M_{mode}"
+        out[key] = _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops)
+        if car is not None:
+            car.check()
+            car.close()
+    return out
+
+
+def _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops) -> List[Dict]:
+    import torch.distributed as dist
+    layers = len(Ls)
     res = []
     for M in ms:
         gen = torch.Generator(device=dev).manual_seed(99 + M)
@@ -258,5 +289,4 @@ def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4,
                     "layer_tokens_per_s": M * layers / t, "roofline_frac": roof / t,
                     "graph": graph is not None})
         del graph
-    return {"tp": world, "layers": layers, "dims": dataclasses.asdict(d), "per_M": res,
-            "note": "attention replaced by the rank's q section of the QKV output"}
+    return res
