@@ -52,9 +52,13 @@ def main():
                 ar(t)
                 ok = torch.equal(t.cpu(), reference(world, n, step))
                 if n * 2 > ar.max_bytes:
-                    # the library collective's summation order is its own: tolerance only
-                    ok = torch.allclose(t.cpu().float(), reference(world, n, step).float(), rtol=1e-2, atol=1e-2)
-                verdict["msgs"].append([n, bool(ok)])
+                    # NCCL sums in its own order with bf16 intermediates: bound the error
+                    # by the magnitudes summed, not by the (possibly cancelling) result
+                    mag = sum(inputs(r, n, step).float().abs() for r in range(world))
+                    err = (t.cpu().float() - reference(world, n, step).float()).abs()
+                    ok = bool(torch.all(err <= mag * 2.0 ** -6 + 1e-6))
+                if not ok:
+                    verdict["msgs"].append(["FAILED size", n])
                 verdict["ok"] &= bool(ok)
             ar.check()
             # CUDA graph: three calls of different sizes captured once, replayed with new data
@@ -76,7 +80,8 @@ def main():
                 for i, b in enumerate(bufs):
                     ok = torch.equal(b.cpu(), reference(world, b.numel(), 100 + 10 * rep + i))
                     verdict["ok"] &= bool(ok)
-                    verdict["msgs"].append([f"graph{rep}.{i}", bool(ok)])
+                    if not ok:
+                        verdict["msgs"].append(["FAILED graph", rep, i])
             ar.check()
             del g
             verdict["calls_custom"], verdict["calls_fallback"] = ar.calls_custom, ar.calls_fallback

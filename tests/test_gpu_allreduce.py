@@ -67,16 +67,16 @@ def _free_port():
     return p
 
 
-def _run_two(mode, tmp_path, timeout=240):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _run(mode, tmp_path, world, timeout=240):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     port = str(_free_port())
     procs, outs = [], []
-    for r in range(2):
+    for r in range(world):
         out = str(tmp_path / f"ar_{mode}_{r}.json")
         outs.append(out)
-        procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "ar_worker.py"), str(r), "2", port, mode, out],
-                                      env=dict(os.environ), start_new_session=True))
+        procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "ar_worker.py"), str(r), str(world), port,
+                                       mode, out], env=dict(os.environ), start_new_session=True))
     try:
         for p in procs:
             p.wait(timeout=timeout)
@@ -88,7 +88,7 @@ def _run_two(mode, tmp_path, timeout=240):
 
 
 def test_two_gpus_parity_graph_and_fallback(tmp_path):
-    vs = _run_two("parity", tmp_path)
+    vs = _run("parity", tmp_path, 2)
     for v in vs:
         assert v["ok"], v
         assert v["calls_custom"] >= 6 and v["calls_fallback"] == 1
@@ -96,6 +96,16 @@ def test_two_gpus_parity_graph_and_fallback(tmp_path):
 
 
 def test_two_gpus_absent_rank(tmp_path):
-    vs = _run_two("absent", tmp_path)
+    vs = _run("absent", tmp_path, 2)
     assert vs[0]["ok"] and any("timed out" in m for m in vs[0]["msgs"]), vs[0]
     assert vs[1]["ok"], vs[1]
+
+
+def test_all_gpus_parity(tmp_path):
+    """Every GPU of the box as one group (3 to 8 ranks)."""
+    world = min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 0
+    if world < 3:
+        pytest.skip("needs three or more GPUs")
+    for v in _run("parity", tmp_path, world):
+        assert v["ok"], v
+        assert v["calls_custom"] >= 6 and v["calls_fallback"] == 1
