@@ -186,6 +186,7 @@ struct w4a8_ar {
     Layout lay{};
     uint8_t* local = nullptr;               // own allocation
     uint8_t* mapped[kMaxRanks] = {};        // peers' allocations opened here
+    bool ipc[kMaxRanks] = {};               // mapped[r] came from cudaIpcOpenMemHandle
     bool opened = false;
 };
 
@@ -235,6 +236,7 @@ int w4a8_ar_open_peers(w4a8_ar* h, const void* handles)
         void* p = nullptr;
         if (cudaIpcOpenMemHandle(&p, m, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return W4A8_ERR_CUDA;
         h->mapped[r] = static_cast<uint8_t*>(p);
+        h->ipc[r] = true;
     }
     h->opened = true;
     return W4A8_OK;
@@ -320,9 +322,10 @@ int w4a8_ar_destroy(w4a8_ar* h)
     if (!h) return W4A8_OK;
     cudaDeviceSynchronize();
     for (int r = 0; r < h->world; ++r)
-        if (r != h->rank && h->mapped[r]) cudaIpcCloseMemHandle(h->mapped[r]);
+        if (h->ipc[r]) cudaIpcCloseMemHandle(h->mapped[r]);
     cudaFree(h->local);
     delete h;
+    cudaGetLastError();          // leave no error pending for the caller's next launch check
     return W4A8_OK;
 }
 
