@@ -323,6 +323,31 @@ def test_config0_full_size(orc):
     _close(orc.bf16_to_f32(_bits(y)), y64)
 
 
+@pytest.mark.parametrize("shape,M", [("gate_up", 8192), ("down", 4096), ("qkv", 8192), ("o", 2048)])
+def test_config2_full_size_sampled_rows(orc, shape, M):
+    """BASELINE config 2 at its largest sizes.  Activation quantisation is per
+    row, so the oracle evaluated on a subset of rows is exact for those rows:
+    sampled rows from every token tile region (first, middle, last) are checked
+    against the float64 reference, and repeated calls must be bit-identical."""
+    from w4a8_b200 import ops
+    from w4a8_b200 import synthetic as syn
+    from w4a8_b200.synthetic import QWQ_SHAPES
+    dev = _dev()
+    K, N = QWQ_SHAPES[shape]
+    gk = 128
+    codes, scale, _ = syn.weight_torch(N, K, gk, 21, dev)
+    pw = ops.prepare_weights(ops.pack_int4_grouped(codes, gk), scale, None, K, gk)
+    x = syn.activation_torch(M, K, 22, dev)
+    y = ops.linear_prepared(x, pw)
+    y2 = ops.linear_prepared(x, pw)
+    assert torch.equal(y, y2)
+    assert ops.workspace_status() == 0
+    rows = sorted({0, 1, 127, 128, M // 2 - 1, M // 2, M // 2 + 77, M - 129, M - 2, M - 1})
+    xb = _bits(x[rows])
+    y64, _ = orc.linear(xb, codes.cpu().numpy(), scale.cpu().numpy(), None, gk, exact=True)
+    _close(orc.bf16_to_f32(_bits(y[rows])), y64)
+
+
 # ------------------------------------------------------------------ reference-compatible GEMM
 
 @pytest.mark.parametrize("M,N,K,gk", [(1, 128, 1024, 1024), (16, 256, 5120, 1024), (20, 128, 1057, 1024),
