@@ -170,6 +170,12 @@ __device__ __forceinline__ void pdl_launch_dependents()
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Pins a value in a register at this point of the program: arithmetic that
+// depends only on the launch shape is then done before a following
+// pdl_wait() (volatile asm statements keep their order) instead of after it.
+__device__ __forceinline__ void pin(int& v) { asm volatile("" : "+r"(v)); }
+__device__ __forceinline__ void pin(int64_t& v) { asm volatile("" : "+l"(v)); }
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols)

@@ -782,16 +782,30 @@ __global__ void prepare_weights_kernel(const PrepareParams p)
 // single CTA finished were stored by the GEMM and are skipped.  Launched
 // right after the GEMM as a programmatic dependent: it waits for the GEMM
 // grid to complete, so every part is visible without fences.
+//
+// Which CTAs hold parts of a tile follows from the launch shape alone, so the
+// integer divisions that find them run before the wait, while the GEMM is
+// still streaming.  A CTA after the first one of a split tile starts its range
+// inside the tile, so its part is in its first-tile slot (flush_tile's side 0);
+// the first CTA's part is there only when its range starts with the tile.
 template <int TT>
 __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, const int nctas)
 {
     pdl_launch_dependents();
-    pdl_wait();
     const int t = blockIdx.x;
     const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
-    const int cf = cta_of_unit(p, tfirst, nctas), cl = cta_of_unit(p, tlast, nctas);
+    int cf = cta_of_unit(p, tfirst, nctas), cl = cta_of_unit(p, tlast, nctas);
     if (cf == cl) return;
-    const int wt = t / p.n_tt, tt = t - wt * p.n_tt;
+    int u0f, u1f;
+    cta_range(p, cf, nctas, u0f, u1f);
+    int side_f = u0f == tfirst ? 0 : 1;
+    int wt = t / p.n_tt;
+    pin(cf);
+    pin(cl);
+    pin(side_f);
+    pin(wt);
+    pdl_wait();
+    const int tt = t - wt * p.n_tt;
     const int row = threadIdx.x;
     const int n = wt * 128 + row;
     __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
@@ -804,13 +818,10 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, 
             float v[4][16];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const float* src = p.partials;
-                bool valid = c + q <= cl;
-                if (valid) {
-                    int u0, u1;
-                    cta_range(p, c + q, nctas, u0, u1);
-                    src = p.partials + static_cast<int64_t>(2 * (c + q) + (t == u0 / p.units_per_tile ? 0 : 1)) * (TT * 128);
-                }
+                const int cc = c + q;
+                const bool valid = cc <= cl;
+                const float* src = valid ? p.partials + static_cast<int64_t>(2 * cc + (cc == cf ? side_f : 0)) * (TT * 128)
+                                         : p.partials;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[q][j] = valid ? __ldcg(src + (c0 + j) * 128 + row) : 0.0f;
             }

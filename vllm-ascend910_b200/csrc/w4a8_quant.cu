@@ -73,7 +73,6 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
     __shared__ int red_i[kQThreads / 32];
 
     pdl_launch_dependents();
-    pdl_wait();
 
     const int row = blockIdx.y;
     const int tid = threadIdx.x;
@@ -84,7 +83,18 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
     const int span = (kOut == kOutKernel) ? p.kb_total * 256 : p.Kpad;
     const bool active = pos < span;
     const bool real_row = row < p.M;
-    const int g = pos / gk;
+    int g = pos / gk;
+    // Output offsets depend on the launch shape only: the integer divisions run
+    // before the wait for the kernel that produces x.
+    int64_t a_off = 0, s_off = 0;
+    if (kOut == kOutKernel) {
+        a_off = gemm_act_tile_offset(row, pos, p.tt, p.kb_total);
+        s_off = (static_cast<int64_t>(row / p.tt) * p.G + g) * p.tt + row % p.tt;
+    }
+    pin(g);
+    pin(a_off);
+    pin(s_off);
+    pdl_wait();
 
     // ---- load 8 elements (positions >= K are the group pad: zero) ----
     float xv[8];
@@ -151,9 +161,8 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
                             (static_cast<uint32_t>(q[6] & 0xFF) << 24);
         const uint32_t hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) |
                             (static_cast<uint32_t>(q[7] & 0xFF) << 24);
-        *reinterpret_cast<uint2*>(p.aq + gemm_act_tile_offset(row, pos, p.tt, p.kb_total)) = make_uint2(lo, hi);
-        if (leader && g < p.G)
-            p.as[(static_cast<int64_t>(row / p.tt) * p.G + g) * p.tt + row % p.tt] = real_row ? s : 0.0f;
+        *reinterpret_cast<uint2*>(p.aq + a_off) = make_uint2(lo, hi);
+        if (leader && g < p.G) p.as[s_off] = real_row ? s : 0.0f;
     } else if (kOut == kOutPublic) {
         if (!real_row) return;
         int8_t* qr = p.q + static_cast<int64_t>(row) * p.K;
