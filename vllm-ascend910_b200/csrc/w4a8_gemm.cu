@@ -472,34 +472,8 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                         tc_fence_after();
                         const uint32_t a_smem = smem_u32(a_stage(sa));
                         const uint32_t a_tmem = tbase + static_cast<uint32_t>(ab * C::ABUF);
-                        if (C::GK <= 256 && g1 - g0 == C::GPU) {
-                            // A whole unit: its slots, groups and K steps are compile-time
-                            // constants, so the MMAs go out as one straight-line block.
-                            // (An MMA issued from a runtime loop iteration costs the
-                            // issuing thread ~250 cycles; unrolled ones ~17.)
-#pragma unroll
-                            for (int s = 0; s < C::GPU / C::CG; ++s) {
-                                if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
-                                tc_fence_after();
-                                const uint32_t d_slot = tbase + C::ACC0 + static_cast<uint32_t>(sl * C::CG * TT);
-#pragma unroll
-                                for (int gi = 0; gi < C::CG; ++gi) {
-                                    const int gl = s * C::CG + gi;
-                                    const int j = gl / C::GPK;                       // k-block within the stage
-                                    const int s0 = (gl % C::GPK) * (C::GK / 32);     // first K step within it
-#pragma unroll
-                                    for (int t = 0; t < C::GK / 32; ++t) {
-                                        const int ks = s0 + t;
-                                        const uint64_t bd = smem_desc_sw128(a_smem + j * C::A_TILE + (ks >> 2) * (TT * 128) + (ks & 3) * 32);
-                                        tc_mma_i8_ts(d_slot + gi * TT, a_tmem + j * 64 + ks * 8, bd, idesc, t == 0 ? 0u : 1u);
-                                    }
-                                }
-                                tc_commit(&bars->accfull[sl]);
-                                if (++sl == C::NACC) { sl = 0; slph ^= 1; }
-                            }
-                            if (!ok) break;
-                        } else if (C::GK <= 256) {
-                            // a ragged last unit: groups g0..g1, CG per accumulator slot
+                        if (C::GK <= 256) {
+                            // the unit is this one stage: groups g0..g1, CG per accumulator slot
                             for (int g = g0; g < g1; ++g) {
                                 const int gl = g - g0, gi = gl % C::CG;
                                 if (gi == 0) {
