@@ -1,6 +1,6 @@
 """Benchmark of the B200 W4A8 mid-group linear layer.
 
-Headline (N=1): the decode sweep of BASELINE config 1 -- the four QwQ-32B
+Headline (N=1): the reference's decode configuration -- the four QwQ-32B
 projections (qkv, o, gate_up, down) at M in {1,4,8,16,32,64}, int4 group-128
 symmetric weights with fp32 per-group scales, bf16 activations quantised per
 (token, group) inside the op.  One step = those 24 linear calls (quantiser +
@@ -14,13 +14,13 @@ divided by the step time.
                  a pinned host->device copy of x and a device->host copy of y
   roofline       the GEMM kernel alone, each launch timed with CUDA events after an
                  L2 flush; achieved = algorithmic bytes / kernel time
-  prefill        BASELINE config 2 subset (M = 2048, 4096): GEMM int8 TOP/s against
+  prefill        the prefill configuration, M = 2048 and 4096: GEMM int8 TOP/s against
                  cuBLAS int8 (torch._int_mm) measured in the same run
   cpu_baseline   the reference's own C++ CPU GEMM (oracle/_ref, compiled from the
                  reference sources) plus the C port of its activation quantiser,
                  on a 1/8-of-N sample of the same sweep, all host threads
-  tp_stack       (N > 1) BASELINE config 4: 4 QwQ-32B decoder-layer linear stacks,
-                 tensor-parallel over the N GPUs with NCCL all-reduce
+  tp_stack       (N > 1) the tensor-parallel configuration: 4 QwQ-32B decoder-layer
+                 linear stacks, tensor-parallel over the N GPUs with NCCL all-reduce
 
 Multi-GPU: one process per GPU (torchrun).  Every rank runs its own replica of
 the sweep (weak scaling; the sweep has no exchange step) and the step time is

@@ -306,7 +306,7 @@ def test_linear_deterministic_and_repeatable(orc):
 
 
 def test_config0_full_size(orc):
-    """M=16 K=5120 N=7168 GK=128, fp32 lognormal scales."""
+    """The reference's CPU-runnable case: M=16 K=5120 N=7168 GK=128, fp32 lognormal scales."""
     from w4a8_b200 import ops
     from w4a8_b200 import synthetic as syn
     dev = _dev()
@@ -325,7 +325,7 @@ def test_config0_full_size(orc):
 
 @pytest.mark.parametrize("shape,M", [("gate_up", 8192), ("down", 4096), ("qkv", 8192), ("o", 2048)])
 def test_config2_full_size_sampled_rows(orc, shape, M):
-    """BASELINE config 2 at its largest sizes.  Activation quantisation is per
+    """The prefill configuration at its largest sizes.  Activation quantisation is per
     row, so the oracle evaluated on a subset of rows is exact for those rows:
     sampled rows from every token tile region (first, middle, last) are checked
     against the float64 reference, and repeated calls must be bit-identical."""
