@@ -115,14 +115,23 @@ W4A8_API int w4a8_linear_gemm_prepared(int64_t M, int64_t K, int64_t N, int32_t 
  *     the array holds (16 MiB covers M <= 64 on 27648 x 7168 weights).
  *   - The first call on a device looks the array up, clears it and waits for
  *     the clear on `stream`: make that first call before any stream capture.
+ *     The same happens again on the first call after the device's context
+ *     was reset (the module, and with it the array, is loaded anew).
  *   - Every call on a device shares the one array: calls that overlap in time
  *     (different streams, threads) race on it and must be serialised by the
- *     caller. */
+ *     caller.
+ *   - A kernel wait that runs out is recorded in the array's status word:
+ *     read (and clear) it with w4a8_fixed_scratch_status. */
 #define W4A8_FIXED_SCRATCH_BYTES ((size_t)16 << 20)
 W4A8_API int w4a8_linear_fixed_scratch(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N,
                                        int32_t group_size, const void* w_packed, const void* w_scale,
                                        int32_t w_scale_dtype, const void* w_zero, void* y, int64_t ldy,
                                        void* stream);
+/* Status word of the current device's fixed scratch, as w4a8_workspace_status
+ * returns it for a workspace (synchronises `stream`; reset != 0 clears it).
+ * No counterpart in the reference.  W4A8_ERR_WORKSPACE when no
+ * w4a8_linear_fixed_scratch call has run in the current context yet. */
+W4A8_API int w4a8_fixed_scratch_status(int32_t reset, void* stream);
 
 /* ---- activation quantiser (fakequant_lab/quant.py:89-141 semantics) ----
  *   a_q       int8 [M, K] natural order

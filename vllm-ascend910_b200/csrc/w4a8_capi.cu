@@ -305,28 +305,79 @@ int check_weights(const void* w_packed, const void* w_scale, int32_t ws_dtype, c
 
 // ---- fixed scratch for w4a8_linear_fixed_scratch ----
 // One statically sized device array per device context (module data, not an
-// allocation).  Its address is looked up once per device with that device
-// current; the whole array is cleared on that first call, after which the
+// allocation).  Its address is looked up with the device current and cached
+// together with the id of the context it belongs to: a context made after a
+// device reset loads the module again, so the array may move and its
+// contents are gone, and the next call looks it up and clears it again.  The
+// whole array is cleared on that first call per context, after which the
 // kernels leave the status word at zero unless a wait runs out.
 __device__ __align__(256) uint8_t g_fixed_scratch[W4A8_FIXED_SCRATCH_BYTES];
 uint8_t* g_fixed_ptr[kMaxDev];
+unsigned long long g_fixed_ctx[kMaxDev];   // cuCtxGetId of the context g_fixed_ptr belongs to
 std::mutex g_fixed_mutex;
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
 
-int fixed_scratch(cudaStream_t st, uint8_t** out)
+// Id of the current context (unique for the life of the process).
+int current_ctx_id(unsigned long long* id)
+{
+    std::call_once(g_ctx_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+    });
+    if (!g_ctx_current || !g_ctx_id) return fail_cuda(cudaErrorNotSupported);
+    CUcontext ctx = nullptr;
+    if (g_ctx_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return fail_cuda(cudaErrorDeviceUninitialized);
+    if (g_ctx_id(ctx, id) != CUDA_SUCCESS) return fail_cuda(cudaErrorDeviceUninitialized);
+    return W4A8_OK;
+}
+
+// The array's address in the current context, or null when no call has
+// looked it up there yet (caller holds g_fixed_mutex).
+int fixed_scratch_cached(int* dev_out, unsigned long long* ctx_out, uint8_t** out)
 {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail_cuda(e);
     if (dev < 0 || dev >= kMaxDev) return W4A8_ERR_DEVICE;
+    unsigned long long ctx = 0;
+    const int rc = current_ctx_id(&ctx);
+    if (rc != W4A8_OK) return rc;
+    *dev_out = dev;
+    *ctx_out = ctx;
+    *out = (g_fixed_ptr[dev] != nullptr && g_fixed_ctx[dev] == ctx) ? g_fixed_ptr[dev] : nullptr;
+    return W4A8_OK;
+}
+
+int fixed_scratch(cudaStream_t st, uint8_t** out)
+{
     std::lock_guard<std::mutex> lock(g_fixed_mutex);
-    if (g_fixed_ptr[dev] == nullptr) {
-        void* ptr = nullptr;
-        if ((e = cudaGetSymbolAddress(&ptr, g_fixed_scratch)) != cudaSuccess) return fail_cuda(e);
+    // The symbol lookup also makes the device's primary context current when
+    // no call has done so yet, so it runs before the context is queried.
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_fixed_scratch);
+    if (e != cudaSuccess) return fail_cuda(e);
+    int dev = 0;
+    unsigned long long ctx = 0;
+    uint8_t* cur = nullptr;
+    const int rc = fixed_scratch_cached(&dev, &ctx, &cur);
+    if (rc != W4A8_OK) return rc;
+    if (cur == nullptr) {
         if ((e = cudaMemsetAsync(ptr, 0, W4A8_FIXED_SCRATCH_BYTES, st)) != cudaSuccess) return fail_cuda(e);
         if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return fail_cuda(e);
         g_fixed_ptr[dev] = static_cast<uint8_t*>(ptr);
+        g_fixed_ctx[dev] = ctx;
+        cur = g_fixed_ptr[dev];
     }
-    *out = g_fixed_ptr[dev];
+    *out = cur;
     return W4A8_OK;
 }
 
@@ -429,6 +480,20 @@ int w4a8_linear_fixed_scratch(const void* x, int64_t M, int64_t K, int64_t ldx, 
     if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
     const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
     return run_gemm(pl, w, y, ldy, false, ws, st);
+}
+
+int w4a8_fixed_scratch_status(int32_t reset, void* stream)
+{
+    uint8_t* ptr = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_fixed_mutex);
+        int dev = 0;
+        unsigned long long ctx = 0;
+        const int rc = fixed_scratch_cached(&dev, &ctx, &ptr);
+        if (rc != W4A8_OK) return rc;
+    }
+    if (ptr == nullptr) return W4A8_ERR_WORKSPACE;   // no call has run in this context
+    return w4a8_workspace_status(ptr, reset, stream);
 }
 
 int w4a8_group_partials(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,

@@ -49,6 +49,7 @@ SIGNATURES = [
      [_i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),
     ("w4a8_linear_fixed_scratch", ctypes.c_int,
      [_p, _i64, _i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _p]),
+    ("w4a8_fixed_scratch_status", ctypes.c_int, [_i32, _p]),
     ("w4a8_quant_act", ctypes.c_int, [_p, _i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p]),
     ("w4a8_midgroup_quant_a", ctypes.c_int, [_p, _i64, _i64, _i32, _i64, _p, _p, _p, _p, _p]),
     ("w4a8_midgroup_gemm_workspace_size", _sz, [_i64, _i64, _i64, _i32]),
