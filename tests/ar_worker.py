@@ -3,7 +3,11 @@
 Run as ``python tests/ar_worker.py RANK WORLD PORT MODE OUTFILE``; writes a JSON
 verdict to OUTFILE.  MODE ``parity``: bit-exact sums against an fp32 rank-order
 reference over many sizes, in place and in a replayed CUDA graph, plus the NCCL
-fallback.  MODE ``absent``: rank 1 stays alive but skips the last call; rank 0's
+fallback.  MODE ``skew``: the reference's barrier gates -- ranks desynchronised
+on purpose (skewed launches, changing values, a 200-call run, graph replays,
+24 live graphs) -- plus a strided and a misaligned message, which take the
+staged form of the one-shot path on one rank while the other passes a dense
+tensor.  MODE ``absent``: rank 1 stays alive but skips the last call; rank 0's
 wait must run out and ``check()`` must raise (no GPU fault, no hang).
 """
 import datetime
@@ -29,6 +33,155 @@ def reference(world, numel, step):
     for r in range(world):
         acc += inputs(r, numel, step).float()
     return acc.to(torch.bfloat16)
+
+
+def skew_value(r, step):
+    """Per-rank message value, exact in bf16 (multiples of 0.25 below 64), with
+    partial sums exact in fp32: a read of last step's slot gives a visibly wrong
+    sum, not a rounding difference."""
+    return (r + 1) * 4.0 + (step % 16) * 0.25
+
+
+def skew_gates(ar, rank, world, dev, verdict):
+    """The ranks are desynchronised on purpose before the calls, so only the
+    kernel's own flags keep them together (the reference's barrier gates,
+    npu_ops/python/test_peer_barrier.py:1-26):
+      0. one message laid out differently on different ranks (staged path);
+      1. skewed launch: rank r sleeps r * 25 ms before its call;
+      2. skewed with the values changing every step;
+      3. 200 calls with a random skew and no host barrier, checked every step;
+      4. one captured graph replayed 20 times with new values and skewed replays;
+      5. 24 graphs of different sizes alive at once, replayed in order."""
+    import random
+    n = 16 * 5120
+    x = torch.empty(n, dtype=torch.bfloat16, device=dev)
+
+    def expect(step):
+        # the kernel sums in fp32 (exact here) and rounds once to bf16
+        return float(torch.tensor(sum(skew_value(r, step) for r in range(world))).to(torch.bfloat16))
+
+    def check(t, step, what):
+        ok = bool(torch.all(t == expect(step)).item())
+        if not ok:
+            verdict["msgs"].append([what, step, float(t.float().min()), float(t.float().max()), expect(step)])
+        verdict["ok"] &= ok
+        return ok
+
+    # 0. the same message as a strided view (rank 0) / a misaligned view (rank 1)
+    #    against a dense tensor elsewhere: every rank must take the one-shot path
+    for step, kind in ((900, "strided"), (901, "misaligned")):
+        ref_t = reference(world, n, step)
+        dense = inputs(rank, n, step).to(dev)
+        if rank == 0 and kind == "strided":
+            big = torch.zeros(n, 2, dtype=torch.bfloat16, device=dev)
+            big[:, 0] = dense
+            t = big[:, 0]
+        elif rank == 1 and kind == "misaligned":
+            raw = torch.zeros(n + 1, dtype=torch.bfloat16, device=dev)
+            t = raw[1:]
+            t.copy_(dense)
+        else:
+            t = dense
+        before = ar.calls_custom
+        ar(t)
+        ok = torch.equal(t.cpu(), ref_t) and ar.calls_custom == before + 1
+        if not ok:
+            verdict["msgs"].append(["layout", kind])
+        verdict["ok"] &= bool(ok)
+    ar.check()
+    # 1. skewed launch
+    x.fill_(skew_value(rank, 1))
+    dist.barrier()
+    time.sleep(0.025 * rank)
+    ar(x)
+    torch.cuda.synchronize()
+    check(x, 1, "skewed launch")
+    # 2. skewed, values change every step
+    for step in range(2, 12):
+        x.fill_(skew_value(rank, step))
+        dist.barrier()
+        time.sleep(0.01 * ((rank + step) % world))
+        ar(x)
+        torch.cuda.synchronize()
+        check(x, step, "skewed changing values")
+    # 3. 200 calls, random skew, no host barrier; a full random message every 10th
+    rng = random.Random(1234 + rank)
+    bad = 0
+    for step in range(12, 212):
+        if step % 10 == 0:
+            t = inputs(rank, n, step).to(dev)
+            if rng.random() < 0.3:
+                time.sleep(rng.random() * 0.005)
+            ar(t)
+            if not torch.equal(t.cpu(), reference(world, n, step)):
+                bad += 1
+            continue
+        x.fill_(skew_value(rank, step))
+        if rng.random() < 0.1:
+            time.sleep(rng.random() * 0.005)
+        ar(x)
+        torch.cuda.synchronize()
+        if not bool(torch.all(x == expect(step)).item()):
+            bad += 1
+    if bad:
+        verdict["ok"] = False
+        verdict["msgs"].append(["long skewed run: wrong steps", bad])
+    verdict["skew_long_steps"] = 200
+    ar.check()
+    # 4. one graph, 20 replays, new values each time, skewed replays
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    x.fill_(skew_value(rank, 0))
+    torch.cuda.synchronize()
+    dist.barrier()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            ar(x)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    for rep in range(20):
+        step = 300 + rep
+        x.fill_(skew_value(rank, step))
+        torch.cuda.synchronize()
+        time.sleep(0.005 * ((rank + rep) % world))
+        g.replay()
+        torch.cuda.synchronize()
+        check(x, step, "graph replay")
+    del g
+    ar.check()
+    # 5. 24 graphs of different sizes alive, replayed in order
+    sizes = [16 * (i + 1) for i in range(4)] + [512, 1024, 2048, 2560, 5120]
+    sizes = (sizes * 3)[:24]
+    bufs, graphs = [], []
+    for m in sizes:
+        b = torch.full((m,), skew_value(rank, 0), dtype=torch.bfloat16, device=dev)
+        ar(b)                                   # warm the size before capturing it
+        torch.cuda.synchronize()
+        dist.barrier()
+        gi = torch.cuda.CUDAGraph()
+        si = torch.cuda.Stream()
+        si.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(si):
+            with torch.cuda.graph(gi, stream=si):
+                ar(b)
+        torch.cuda.current_stream().wait_stream(si)
+        bufs.append(b)                          # a graph replays against the captured address
+        graphs.append(gi)
+    torch.cuda.synchronize()
+    for rnd in range(2):
+        for i, (b, gi) in enumerate(zip(bufs, graphs)):
+            step = 400 + 30 * rnd + i
+            b.fill_(skew_value(rank, step))
+            torch.cuda.synchronize()
+            dist.barrier()
+            gi.replay()
+            torch.cuda.synchronize()
+            check(b, step, f"graph {i} of {len(graphs)} alive")
+    del graphs
+    ar.check()
+    verdict["calls_custom"], verdict["calls_fallback"] = ar.calls_custom, ar.calls_fallback
 
 
 def main():
@@ -131,6 +284,8 @@ def main():
                     verdict["us"][f"{name}_m{rows}"] = e0.elapsed_time(e1) * 1e3 / 250
                     del g
             ar.check()
+        elif mode == "skew":
+            skew_gates(ar, rank, world, dev, verdict)
         elif mode == "absent":
             t = inputs(rank, 5120, 0).to(dev)
             ar(t)

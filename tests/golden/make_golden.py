@@ -206,9 +206,12 @@ def weight_cases(reference, out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("W4A8_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("W4A8_REFERENCE"),
+                    help="the reference checkout (default: $W4A8_REFERENCE)")
     ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
     args = ap.parse_args()
+    if not args.reference or not os.path.isdir(args.reference):
+        ap.error("name the reference checkout with --reference or $W4A8_REFERENCE")
     sys.path.insert(0, args.reference)
     from fakequant_lab import fake_linear as fl
     from fakequant_lab import quant

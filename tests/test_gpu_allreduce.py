@@ -95,6 +95,20 @@ def test_two_gpus_parity_graph_and_fallback(tmp_path):
     print({k: v for k, v in vs[0].items() if k.startswith("us_")})
 
 
+def test_two_gpus_skewed_barrier_gates(tmp_path):
+    """Ranks desynchronised on purpose: only the kernel's flags keep them together."""
+    for v in _run("skew", tmp_path, 2):
+        assert v["ok"], v
+
+
+def test_all_gpus_skewed_barrier_gates(tmp_path):
+    world = min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 0
+    if world < 3:
+        pytest.skip("needs three or more GPUs")
+    for v in _run("skew", tmp_path, world, timeout=420):
+        assert v["ok"], v
+
+
 def test_two_gpus_absent_rank(tmp_path):
     vs = _run("absent", tmp_path, 2)
     assert vs[0]["ok"] and any("timed out" in m for m in vs[0]["msgs"]), vs[0]

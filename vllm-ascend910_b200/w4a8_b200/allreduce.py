@@ -25,10 +25,20 @@ from . import _lib
 DEFAULT_MAX_BYTES = 1 << 20          # M <= 64 at hidden 5120 (640 KB) fits
 
 
-def eligible(numel: int, dtype: torch.dtype, contiguous: bool, data_ptr: int, max_bytes: int) -> bool:
-    """Whether a tensor can take the one-shot path (else the NCCL fallback)."""
-    return (dtype == torch.bfloat16 and contiguous and numel > 0 and numel % 8 == 0
-            and numel * 2 <= max_bytes and data_ptr % 16 == 0)
+def eligible(numel: int, dtype: torch.dtype, max_bytes: int) -> bool:
+    """Whether a tensor takes the one-shot path (else the NCCL fallback).
+
+    Only values every rank shares decide (the message's element count and
+    dtype, and the group's byte limit): ranks that chose differently would
+    wait on each other in two different collectives.  A tensor's own layout
+    (strides, address) may differ between ranks, so it never decides the path;
+    a tensor the kernel cannot take as it is goes through a staging buffer."""
+    return dtype == torch.bfloat16 and numel > 0 and numel % 8 == 0 and numel * 2 <= max_bytes
+
+
+def direct(t: torch.Tensor) -> bool:
+    """Whether the kernel can reduce ``t`` in place (dense and 16-byte aligned)."""
+    return t.is_contiguous() and t.data_ptr() % 16 == 0
 
 
 class _Handle:
@@ -87,17 +97,29 @@ class CustomAllReduce:
             dist.all_gather_object(handles, self._h.ipc_handle(), group=group)
             self._h.open_peers(handles)
         dist.barrier(group=group)
+        # staging for eligible tensors the kernel cannot take in place (a view
+        # with strides, or an address off the 16-byte grid); made here so that
+        # calls inside CUDA graph capture allocate nothing
+        self._stage = torch.empty(max_bytes // 2, dtype=torch.bfloat16, device=self.device)
         self.calls_custom = 0
+        self.calls_staged = 0
         self.calls_fallback = 0
 
     def fits(self, t: torch.Tensor) -> bool:
-        return eligible(t.numel(), t.dtype, t.is_contiguous(), t.data_ptr(), self.max_bytes)
+        return eligible(t.numel(), t.dtype, self.max_bytes)
 
     def __call__(self, t: torch.Tensor) -> None:
         if self.world == 1:
             return
         if self.fits(t):
-            self._h.allreduce(t, t)
+            if direct(t):
+                self._h.allreduce(t, t)
+            else:
+                st = self._stage[:t.numel()]
+                st.view(t.shape).copy_(t)
+                self._h.allreduce(st, st)
+                t.copy_(st.view(t.shape))
+                self.calls_staged += 1
             self.calls_custom += 1
         else:
             import torch.distributed as dist

@@ -7,7 +7,9 @@ nothing here synchronises, so every op is CUDA-graph capturable once its
 workspace exists.
 
 Workspaces: each device keeps one zero-initialised scratch buffer, grown on
-demand outside graph capture (the kernels leave it reusable).
+demand outside graph capture (the kernels leave it reusable).  A buffer that
+is outgrown stays allocated for the life of the process: a CUDA graph captured
+while it was current keeps writing to it on every replay.
 """
 from __future__ import annotations
 
@@ -19,6 +21,11 @@ from . import _lib
 
 GROUP = 1024          # the reference op's compile-time group size (w4a8_ops.py:60)
 _WS: Dict[int, torch.Tensor] = {}
+# Every buffer ever handed out per device, current one last.  Graphs captured
+# earlier hold the addresses of outgrown buffers; freeing those would let the
+# caching allocator give their memory to other tensors that the replays then
+# overwrite.
+_WS_ALL: Dict[int, List[torch.Tensor]] = {}
 
 
 def num_groups(K: int, group_size: int = GROUP) -> int:
@@ -73,16 +80,25 @@ def workspace(nbytes: int, device: torch.device) -> Tuple[int, int]:
                 "run the op once eagerly with the largest shape first")
         buf = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
         _WS[key] = buf
+        _WS_ALL.setdefault(key, []).append(buf)
     base = buf.data_ptr()
     aligned = (base + 1023) & ~1023
     return aligned, buf.numel() - (aligned - base)
 
 
 def workspace_status(device: Optional[torch.device] = None, reset: bool = True) -> int:
-    """Device status word of this stream's workspace (0 = no kernel reported a failure)."""
+    """Device status word of this device's workspaces (0 = no kernel reported a
+    failure): the first non-zero word among the current buffer and every
+    outgrown one (graphs captured earlier still write to those)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
-    ptr, _ = workspace(0, device)
-    return _lib.lib().w4a8_workspace_status(ptr, 1 if reset else 0, _stream(device))
+    workspace(0, device)
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    status = 0
+    for buf in _WS_ALL.get(key, []):
+        ptr = (buf.data_ptr() + 1023) & ~1023
+        v = _lib.lib().w4a8_workspace_status(ptr, 1 if reset else 0, _stream(device))
+        status = status or v
+    return status
 
 
 def _check(cond: bool, msg: str) -> None:
