@@ -72,6 +72,21 @@ W4A8_API int w4a8_linear(const void* x, int64_t M, int64_t K, int64_t ldx, int64
                 const void* w_zero, void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/* ---- the down projection with the SwiGLU activation applied to its input ----
+ * y = bf16(silu(gate) * up) @ W^T for gu = [gate | up], bf16 [M, ldx] with
+ * ldx >= 2K: gate = columns [0, K), up = columns [K, 2K) (vLLM's
+ * MergedColumnParallelLinear output order).  silu(g) = g / (1 + exp(-g)) and
+ * the product are computed in fp32 and rounded to bf16 before quantisation,
+ * as the reference's layer does in torch before its quant op
+ * (F.silu(g) * u in npu_ops/python/bench_decode_layer.py:81; torch_npu.npu_swiglu
+ * in npu_ops/python/bench_decode_graph.py:64), so no [M, K] activation tensor
+ * and no elementwise kernel sit between gate_up and down.  Otherwise as
+ * w4a8_linear (same weights, workspace and rules; K is the down projection's). */
+W4A8_API int w4a8_linear_swiglu(const void* gu, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t group_size,
+                                const void* w_packed, const void* w_scale, int32_t w_scale_dtype,
+                                const void* w_zero, void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* The two halves of w4a8_linear, for callers that quantise once and reuse the
  * quantised activation, or time the GEMM alone.  w4a8_linear_gemm reads the
  * activation w4a8_linear_quant left in the same workspace (same M, K). */
@@ -97,6 +112,11 @@ W4A8_API int w4a8_prepare_weights(const void* w_packed, const void* w_scale, int
 W4A8_API int w4a8_linear_prepared(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t group_size,
                                   const void* prepared, int32_t w_scale_dtype, int32_t has_zero, void* y,
                                   int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+/* w4a8_linear_swiglu on prepared weights. */
+W4A8_API int w4a8_linear_prepared_swiglu(const void* gu, int64_t M, int64_t K, int64_t ldx, int64_t N,
+                                         int32_t group_size, const void* prepared, int32_t w_scale_dtype,
+                                         int32_t has_zero, void* y, int64_t ldy, void* workspace,
+                                         size_t workspace_bytes, void* stream);
 /* The GEMM half of w4a8_linear_prepared (after w4a8_linear_quant on the same workspace). */
 W4A8_API int w4a8_linear_gemm_prepared(int64_t M, int64_t K, int64_t N, int32_t group_size, const void* prepared,
                                        int32_t w_scale_dtype, int32_t has_zero, void* y, int64_t ldy,

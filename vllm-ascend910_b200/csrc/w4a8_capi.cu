@@ -142,12 +142,15 @@ int check_common(int64_t M, int64_t N, int64_t K, int32_t gk)
     return W4A8_OK;
 }
 
-// Quantise x into the GEMM's operand order inside the workspace.
-int run_quant_kernel_layout(const Plan& pl, const void* x, int64_t ldx, uint8_t* ws, cudaStream_t st)
+// Quantise x (or, with swiglu, bf16(silu(gate) * up) of x = [gate | up]) into
+// the GEMM's operand order inside the workspace.
+int run_quant_kernel_layout(const Plan& pl, const void* x, int64_t ldx, uint8_t* ws, cudaStream_t st,
+                            bool swiglu = false)
 {
     QuantParams q{};
     q.x = static_cast<const uint16_t*>(x);
     q.ldx = ldx;
+    q.swiglu = swiglu ? 1 : 0;
     q.M = static_cast<int>(pl.M);
     q.K = static_cast<int>(pl.K);
     q.Kpad = static_cast<int>(pl.Kpad);
@@ -381,6 +384,49 @@ int fixed_scratch(cudaStream_t st, uint8_t** out)
     return W4A8_OK;
 }
 
+int linear_impl(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk, const void* w_packed,
+                const void* w_scale, int32_t ws_dtype, const void* w_zero, void* y, int64_t ldy, void* workspace,
+                size_t workspace_bytes, void* stream, bool swiglu)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < (swiglu ? 2 * K : K) || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if ((rc = check_weights(w_packed, w_scale, ws_dtype, w_zero)) != W4A8_OK) return rc;
+    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st, swiglu)) != W4A8_OK) return rc;
+    const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
+    return run_gemm(pl, w, y, ldy, false, ws, st);
+}
+
+int linear_prepared_impl(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
+                         const void* prepared, int32_t ws_dtype, int32_t has_zero, void* y, int64_t ldy,
+                         void* workspace, size_t workspace_bytes, void* stream, bool swiglu)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < (swiglu ? 2 * K : K) || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if (!prepared || !aligned(prepared, 256)) return W4A8_ERR_INVALID;
+    if (ws_dtype != W4A8_DTYPE_BF16 && ws_dtype != W4A8_DTYPE_F32) return W4A8_ERR_UNSUPPORTED;
+    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st, swiglu)) != W4A8_OK) return rc;
+    const Weights w{nullptr, nullptr, nullptr, static_cast<const uint8_t*>(prepared), has_zero != 0, ws_dtype};
+    return run_gemm(pl, w, y, ldy, false, ws, st);
+}
+
 }  // namespace
 
 extern "C" {
@@ -443,21 +489,16 @@ int w4a8_linear(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int
                 const void* w_scale, int32_t ws_dtype, const void* w_zero, void* y, int64_t ldy, void* workspace,
                 size_t workspace_bytes, void* stream)
 {
-    int rc = check_common(M, N, K, gk);
-    if (rc != W4A8_OK) return rc;
-    if (M == 0) return W4A8_OK;
-    if (!x || ldx < K || !aligned(x, 2)) return W4A8_ERR_INVALID;
-    if ((rc = check_weights(w_packed, w_scale, ws_dtype, w_zero)) != W4A8_OK) return rc;
-    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
-    int sms = 0;
-    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
-    const Plan pl = make_plan(M, N, K, gk, sms);
-    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
-    const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
-    return run_gemm(pl, w, y, ldy, false, ws, st);
+    return linear_impl(x, M, K, ldx, N, gk, w_packed, w_scale, ws_dtype, w_zero, y, ldy, workspace,
+                       workspace_bytes, stream, false);
+}
+
+int w4a8_linear_swiglu(const void* gu, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
+                       const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero, void* y,
+                       int64_t ldy, void* workspace, size_t workspace_bytes, void* stream)
+{
+    return linear_impl(gu, M, K, ldx, N, gk, w_packed, w_scale, ws_dtype, w_zero, y, ldy, workspace,
+                       workspace_bytes, stream, true);
 }
 
 int w4a8_linear_fixed_scratch(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
@@ -647,22 +688,16 @@ int w4a8_linear_prepared(const void* x, int64_t M, int64_t K, int64_t ldx, int64
                          int32_t ws_dtype, int32_t has_zero, void* y, int64_t ldy, void* workspace,
                          size_t workspace_bytes, void* stream)
 {
-    int rc = check_common(M, N, K, gk);
-    if (rc != W4A8_OK) return rc;
-    if (M == 0) return W4A8_OK;
-    if (!x || ldx < K || !aligned(x, 2)) return W4A8_ERR_INVALID;
-    if (!prepared || !aligned(prepared, 256)) return W4A8_ERR_INVALID;
-    if (ws_dtype != W4A8_DTYPE_BF16 && ws_dtype != W4A8_DTYPE_F32) return W4A8_ERR_UNSUPPORTED;
-    if (!y || ldy < N || !aligned(y, 2)) return W4A8_ERR_INVALID;
-    int sms = 0;
-    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
-    const Plan pl = make_plan(M, N, K, gk, sms);
-    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
-    const Weights w{nullptr, nullptr, nullptr, static_cast<const uint8_t*>(prepared), has_zero != 0, ws_dtype};
-    return run_gemm(pl, w, y, ldy, false, ws, st);
+    return linear_prepared_impl(x, M, K, ldx, N, gk, prepared, ws_dtype, has_zero, y, ldy, workspace,
+                                workspace_bytes, stream, false);
+}
+
+int w4a8_linear_prepared_swiglu(const void* gu, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
+                                const void* prepared, int32_t ws_dtype, int32_t has_zero, void* y, int64_t ldy,
+                                void* workspace, size_t workspace_bytes, void* stream)
+{
+    return linear_prepared_impl(gu, M, K, ldx, N, gk, prepared, ws_dtype, has_zero, y, ldy, workspace,
+                                workspace_bytes, stream, true);
 }
 
 int w4a8_linear_gemm_prepared(int64_t M, int64_t K, int64_t N, int32_t gk, const void* prepared, int32_t ws_dtype,

@@ -14,6 +14,7 @@ struct QuantParams {
     const uint16_t* x;   // bf16 bits [M, ldx]
     int64_t ldx;
     int M, K, Kpad, G, gk;
+    int swiglu;          // x holds [gate | up] ([M, 2K] within ldx): quantise bf16(silu(gate) * up)
     int rows;            // rows to emit: M, or Mp for the MSD form
     int vec_ok;          // 16-byte vector loads are legal for this x
     // kOutKernel: the GEMM's activation tiles (see gemm_act_tile_offset)

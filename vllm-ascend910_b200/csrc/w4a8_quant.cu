@@ -59,6 +59,31 @@ __device__ __forceinline__ uint16_t scale_bits_from_amax(float amax)
     return sb;
 }
 
+// The layer stack's activation on one element: bf16(silu(g) * u) with
+// silu(g) = g / (1 + exp(-g)) in fp32, as the reference computes it in torch
+// (F.silu(g) * u, npu_ops/python/bench_decode_layer.py:81) before quantising.
+__device__ __forceinline__ float swiglu_bf16(float g, float u)
+{
+    const float a = __fmul_rn(__fdiv_rn(g, 1.0f + expf(-g)), u);
+    return bf16_bits_to_f32(f32_to_bf16_bits(a));
+}
+
+__device__ __forceinline__ void load8_bf16(const uint16_t* xr, int pos, int K, bool vec, float (&v)[8])
+{
+    if (vec && pos + 8 <= K) {
+        const uint4 q = *reinterpret_cast<const uint4*>(xr + pos);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = pos + i < K ? bf16_bits_to_f32(xr[pos + i]) : 0.0f;
+    }
+}
+
 __device__ __forceinline__ int quant_one(float xv, float s)
 {
     float r = rintf(__fdiv_rn(xv, s));
@@ -102,18 +127,12 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
     for (int i = 0; i < 8; ++i) xv[i] = 0.0f;
     if (active && real_row && pos < p.Kpad) {
         const uint16_t* xr = p.x + static_cast<int64_t>(row) * p.ldx;
-        if (p.vec_ok && pos + 8 <= p.K) {
-            const uint4 v = *reinterpret_cast<const uint4*>(xr + pos);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        load8_bf16(xr, pos, p.K, p.vec_ok, xv);
+        if (p.swiglu) {
+            float uv[8];
+            load8_bf16(xr + p.K, pos, p.K, p.vec_ok, uv);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                xv[2 * i] = __uint_as_float(w[i] << 16);
-                xv[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (pos + i < p.K) xv[i] = bf16_bits_to_f32(xr[pos + i]);
+            for (int i = 0; i < 8; ++i) xv[i] = swiglu_bf16(xv[i], uv[i]);
         }
     }
 

@@ -38,12 +38,16 @@ SIGNATURES = [
     ("w4a8_linear_workspace_size", _sz, [_i64, _i64, _i64, _i32]),
     ("w4a8_linear", ctypes.c_int,
      [_p, _i64, _i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _p, _sz, _p]),
+    ("w4a8_linear_swiglu", ctypes.c_int,
+     [_p, _i64, _i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _p, _sz, _p]),
     ("w4a8_linear_quant", ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i32, _p, _sz, _p]),
     ("w4a8_linear_gemm", ctypes.c_int,
      [_i64, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _p, _sz, _p]),
     ("w4a8_prepared_weights_size", _sz, [_i64, _i64, _i32, _i32, _i32]),
     ("w4a8_prepare_weights", ctypes.c_int, [_p, _p, _i32, _p, _i64, _i64, _i32, _p, _sz, _p]),
     ("w4a8_linear_prepared", ctypes.c_int,
+     [_p, _i64, _i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),
+    ("w4a8_linear_prepared_swiglu", ctypes.c_int,
      [_p, _i64, _i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),
     ("w4a8_linear_gemm_prepared", ctypes.c_int,
      [_i64, _i64, _i64, _i32, _p, _i32, _i32, _p, _i64, _p, _sz, _p]),

@@ -63,6 +63,41 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_of(t: torch.Tensor) -> int:
+    """The current stream of t's device, as a cudaStream_t value (the raw lookup
+    skips the Python Stream object that current_stream() builds per call)."""
+    if _raw_stream is not None:
+        return _raw_stream(t.get_device())
+    return _stream(t.device)
+
+
+# workspace bytes per (M, N, K, group size): a pure function of the shape and
+# the device's SM count (one process drives one kind of GPU)
+_WS_BYTES: Dict[Tuple[int, int, int, int], int] = {}
+
+
+def _ws_bytes(M: int, N: int, K: int, group_size: int) -> int:
+    key = (M, N, K, group_size)
+    n = _WS_BYTES.get(key)
+    if n is None:
+        n = _lib.lib().w4a8_linear_workspace_size(M, N, K, group_size)
+        _WS_BYTES[key] = n
+    return n
+
+
+def _act_k(x: torch.Tensor, act: Optional[str]) -> int:
+    """The linear's K for input x: its last dimension, or half of it for
+    act="swiglu" (x = [gate | up])."""
+    if act is None:
+        return x.shape[-1]
+    _check(act == "swiglu", f"w4a8 linear: unknown activation {act!r} (None or 'swiglu')")
+    _check(x.shape[-1] % 2 == 0, "w4a8 linear: act='swiglu' needs x = [gate | up] with an even last dimension")
+    return x.shape[-1] // 2
+
+
 def workspace(nbytes: int, device: torch.device) -> Tuple[int, int]:
     """(aligned pointer, usable bytes) of this device's scratch buffer.
 
@@ -212,13 +247,17 @@ def _check_weight(w_packed, w_scale, w_zero, K, group_size):
 
 
 def linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor,
-           w_zero: Optional[torch.Tensor], group_size: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+           w_zero: Optional[torch.Tensor], group_size: int, out: Optional[torch.Tensor] = None,
+           act: Optional[str] = None) -> torch.Tensor:
     """y = x @ W^T for packed int4 W with per-group scales (and zero points):
-    the activation is quantised per (token, group) inside the op."""
+    the activation is quantised per (token, group) inside the op.  With
+    act="swiglu", x = [gate | up] and the op computes bf16(silu(gate) * up) @ W^T
+    (the activation is applied by the quantiser as it reads x)."""
     _check(x.dtype == torch.bfloat16, "w4a8 linear: x must be bfloat16")
     _check_cuda(x, w_packed, w_scale, w_zero)
-    lead, K = x.shape[:-1], x.shape[-1]
-    x2 = x.reshape(-1, K)
+    K = _act_k(x, act)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
     M = x2.shape[0]
@@ -227,12 +266,12 @@ def linear(x: torch.Tensor, w_packed: torch.Tensor, w_scale: torch.Tensor,
     if M == 0:
         return y.reshape(*lead, N)
     L = _lib.lib()
-    ws, wsb = workspace(L.w4a8_linear_workspace_size(M, N, K, group_size), x.device)
+    ws, wsb = workspace(_ws_bytes(M, N, K, group_size), x.device)
     sd = _lib.DTYPE_F32 if w_scale.dtype == torch.float32 else _lib.DTYPE_BF16
-    rc = L.w4a8_linear(x2.data_ptr(), M, K, x2.stride(0), N, group_size, w_packed.data_ptr(),
-                       w_scale.data_ptr(), sd, _ptr(w_zero), y.data_ptr(), y.stride(0), ws, wsb,
-                       _stream(x.device))
-    _lib.check(rc, "w4a8_linear")
+    fn = L.w4a8_linear if act is None else L.w4a8_linear_swiglu
+    rc = fn(x2.data_ptr(), M, K, x2.stride(0), N, group_size, w_packed.data_ptr(),
+            w_scale.data_ptr(), sd, _ptr(w_zero), y.data_ptr(), y.stride(0), ws, wsb, _stream_of(x2))
+    _lib.check(rc, "w4a8_linear" if act is None else "w4a8_linear_swiglu")
     return y.reshape(*lead, N)
 
 
@@ -240,7 +279,7 @@ def linear_quant(x2: torch.Tensor, N: int, group_size: int) -> None:
     """First half of ``linear``: quantise x into this stream's workspace."""
     M, K = x2.shape
     L = _lib.lib()
-    ws, wsb = workspace(L.w4a8_linear_workspace_size(M, N, K, group_size), x2.device)
+    ws, wsb = workspace(_ws_bytes(M, N, K, group_size), x2.device)
     rc = L.w4a8_linear_quant(x2.data_ptr(), M, K, x2.stride(0), N, group_size, ws, wsb, _stream(x2.device))
     _lib.check(rc, "w4a8_linear_quant")
 
@@ -291,31 +330,41 @@ def prepare_weights(w_packed: torch.Tensor, w_scale: torch.Tensor, w_zero: Optio
     return pw
 
 
-def linear_prepared(x: torch.Tensor, pw: PreparedWeight, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``linear`` on prepared weights (bit-identical results)."""
-    _check(x.dtype == torch.bfloat16, "w4a8 linear: x must be bfloat16")
-    _check_cuda(x, pw.buf)
-    lead, K = x.shape[:-1], x.shape[-1]
-    _check(K == pw.K, f"w4a8 linear: x has K={K}, weights were prepared for K={pw.K}")
-    x2 = x.reshape(-1, K)
+def linear_prepared(x: torch.Tensor, pw: PreparedWeight, out: Optional[torch.Tensor] = None,
+                    act: Optional[str] = None) -> torch.Tensor:
+    """``linear`` on prepared weights (bit-identical results).  The per-call
+    host work is kept to the checks the kernels need, one cached workspace
+    lookup and one C call: decode steps make many small calls."""
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError("w4a8 linear: x must be bfloat16")
+    if not x.is_cuda or x.device != pw.buf.device:
+        raise RuntimeError("w4a8 ops need CUDA tensors on the weights' device (there is no CPU implementation)")
+    K = pw.K
+    if x.shape[-1] != (K if act is None else 2 * K):
+        _act_k(x, act)
+        raise RuntimeError(f"w4a8 linear: x has last dimension {x.shape[-1]}, weights were prepared for K={K}"
+                           + (" (act='swiglu' takes [gate | up] = 2K)" if act else ""))
+    x2 = x if x.dim() == 2 else x.reshape(-1, x.shape[-1])
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
     M, N = x2.shape[0], pw.N
     y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     if M == 0:
-        return y.reshape(*lead, N)
+        return y.reshape(*x.shape[:-1], N)
+    ws, wsb = workspace(_ws_bytes(M, N, K, pw.group_size), x.device)
     L = _lib.lib()
-    ws, wsb = workspace(L.w4a8_linear_workspace_size(M, N, K, pw.group_size), x.device)
-    rc = L.w4a8_linear_prepared(x2.data_ptr(), M, K, x2.stride(0), N, pw.group_size, pw.ptr(), pw.ws_dtype,
-                                1 if pw.has_zero else 0, y.data_ptr(), y.stride(0), ws, wsb, _stream(x.device))
-    _lib.check(rc, "w4a8_linear_prepared")
-    return y.reshape(*lead, N)
+    fn = L.w4a8_linear_prepared if act is None else L.w4a8_linear_prepared_swiglu
+    rc = fn(x2.data_ptr(), M, K, x2.stride(0), N, pw.group_size, pw.ptr(), pw.ws_dtype,
+            1 if pw.has_zero else 0, y.data_ptr(), y.stride(0), ws, wsb, _stream_of(x2))
+    if rc != 0:
+        _lib.check(rc, "w4a8_linear_prepared" if act is None else "w4a8_linear_prepared_swiglu")
+    return y if x.dim() == 2 else y.reshape(*x.shape[:-1], N)
 
 
 def linear_gemm_prepared(M: int, pw: PreparedWeight, y: torch.Tensor) -> None:
     """Second half of ``linear_prepared`` after ``linear_quant(x2, pw.N, pw.group_size)``."""
     L = _lib.lib()
-    ws, wsb = workspace(L.w4a8_linear_workspace_size(M, pw.N, pw.K, pw.group_size), y.device)
+    ws, wsb = workspace(_ws_bytes(M, pw.N, pw.K, pw.group_size), y.device)
     rc = L.w4a8_linear_gemm_prepared(M, pw.K, pw.N, pw.group_size, pw.ptr(), pw.ws_dtype,
                                      1 if pw.has_zero else 0, y.data_ptr(), y.stride(0), ws, wsb,
                                      _stream(y.device))

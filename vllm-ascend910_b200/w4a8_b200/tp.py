@@ -156,6 +156,20 @@ def build_layers(n_layers: int, rank: int, tp: int, device, d: Dims = QWQ, seed:
 
 Linear = Callable[[torch.Tensor, ShardWeights], torch.Tensor]
 AllReduce = Callable[[torch.Tensor], None]
+# gu [M, 2f] = [gate | up] -> linear(bf16(silu(gate) * up), w): the down projection
+# with the activation function applied to its input
+SwigluLinear = Callable[[torch.Tensor, ShardWeights], torch.Tensor]
+
+
+def swiglu(gu: torch.Tensor) -> torch.Tensor:
+    """bf16(silu(gate) * up) in fp32 for gu = [gate | up] (the stack's activation)."""
+    f = gu.shape[-1] // 2
+    return (torch.nn.functional.silu(gu[..., :f].float()) * gu[..., f:].float()).to(torch.bfloat16)
+
+
+def composed_swiglu_linear(linear: Linear) -> SwigluLinear:
+    """The activation as its own step, then the linear (the CPU tests' form)."""
+    return lambda gu, w: linear(swiglu(gu), w)
 
 
 def cuda_linear(x: torch.Tensor, w: ShardWeights) -> torch.Tensor:
@@ -165,24 +179,59 @@ def cuda_linear(x: torch.Tensor, w: ShardWeights) -> torch.Tensor:
     return ops.linear(x, w.packed, w.scale, None, GK)
 
 
+def cuda_swiglu_linear(gu: torch.Tensor, w: ShardWeights) -> torch.Tensor:
+    """The down projection with silu(gate) * up computed by the op's activation
+    quantiser as it reads gu: no elementwise kernels and no [M, f] activation
+    tensor between gate_up and down."""
+    from . import ops
+    if w.prepared is not None:
+        return ops.linear_prepared(gu, w.prepared, act="swiglu")
+    return ops.linear(gu, w.packed, w.scale, None, GK, act="swiglu")
+
+
 def layer_forward(h: torch.Tensor, L: LayerShard, tp: int, linear: Linear, allreduce: AllReduce,
-                  d: Dims = QWQ) -> torch.Tensor:
+                  d: Dims = QWQ, swiglu_linear: Optional[SwigluLinear] = None) -> torch.Tensor:
+    swiglu_linear = swiglu_linear or composed_swiglu_linear(linear)
     qkv = linear(h, L.qkv)
     att = qkv[:, : d.hidden // tp]                     # attention stand-in: the rank's q section
     o = linear(att, L.o)
     allreduce(o)
     gu = linear(o, L.gate_up)
-    f = d.ffn // tp
-    act = (torch.nn.functional.silu(gu[:, :f].float()) * gu[:, f:].float()).to(torch.bfloat16)
-    dn = linear(act, L.down)
+    dn = swiglu_linear(gu, L.down)
     allreduce(dn)
     return dn
 
 
 def stack_forward(h: torch.Tensor, layers: Sequence[LayerShard], tp: int, linear: Linear,
-                  allreduce: AllReduce, d: Dims = QWQ) -> torch.Tensor:
+                  allreduce: AllReduce, d: Dims = QWQ,
+                  swiglu_linear: Optional[SwigluLinear] = None) -> torch.Tensor:
     for L in layers:
-        h = layer_forward(h, L, tp, linear, allreduce, d)
+        h = layer_forward(h, L, tp, linear, allreduce, d, swiglu_linear)
+    return h
+
+
+def _sum_bf16(parts: Sequence[torch.Tensor]) -> torch.Tensor:
+    """fp32 sum in rank order, rounded once to bf16: the one-shot all-reduce's arithmetic."""
+    acc = parts[0].float()
+    for p in parts[1:]:
+        acc = acc + p.float()
+    return acc.to(torch.bfloat16)
+
+
+def emulated_stack_forward(h: torch.Tensor, ranks: Sequence[Sequence[LayerShard]], linear: Linear,
+                           d: Dims = QWQ, swiglu_linear: Optional[SwigluLinear] = None) -> torch.Tensor:
+    """The tp-way sharded stack with every rank's shard on one device: the ranks
+    run each layer in lockstep and each all-reduce is the fp32 rank-order sum
+    of their partial outputs.  The same sharding and per-rank linears as the
+    multi-process stack, so it checks the tensor-parallel arithmetic at TP
+    shapes on one GPU."""
+    tp = len(ranks)
+    swiglu_linear = swiglu_linear or composed_swiglu_linear(linear)
+    for li in range(len(ranks[0])):
+        Ls = [r[li] for r in ranks]
+        att = [linear(h, L.qkv)[:, : d.hidden // tp] for L in Ls]
+        o = _sum_bf16([linear(a, L.o) for a, L in zip(att, Ls)])
+        h = _sum_bf16([swiglu_linear(linear(o, L.gate_up), L.down) for L in Ls])
     return h
 
 
