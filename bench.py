@@ -10,21 +10,32 @@ algorithmic HBM GB/s: sum over calls of N*K/2 + G*N*4 + M*K*2 + M*N*2 bytes,
 divided by the step time.
 
   value          device time of K CUDA-graph replays of the step (inputs resident)
-  e2e            the same step through the public op with host buffers: per call
-                 a pinned host->device copy of x and a device->host copy of y
+  e2e            the same step through the public op with host buffers: per step one
+                 pinned host->device copy of the 24 inputs, the 24 eager op calls and
+                 one device->host copy of the 24 outputs, copies overlapped with
+                 neighbouring steps' compute on their own streams
   roofline       the GEMM kernel alone, each launch timed with CUDA events after an
-                 L2 flush; achieved = algorithmic bytes / kernel time
-  prefill        the prefill configuration, M = 2048 and 4096: GEMM int8 TOP/s against
-                 cuBLAS int8 (torch._int_mm) measured in the same run
+                 L2 flush; achieved = algorithmic bytes / kernel time.  Timed alone
+                 and cold, a launch pays the pipeline fill that the chained step
+                 overlaps with the previous call, so the per-call sum can exceed the
+                 step time
+  prefill        the prefill configuration, M = 1024 ... 8192: GEMM int8 TOP/s against
+                 cuBLAS int8 (torch._int_mm) measured in the same run; `value` over
+                 M >= 2048, the regime of the target
+  config3        group size {64, 128, 256} x {sym, asym} on gate_up / down: GB/s at
+                 M = 16, TOP/s at M = 4096
   cpu_baseline   the reference's own C++ CPU GEMM (oracle/_ref, compiled from the
                  reference sources) plus the C port of its activation quantiser,
                  on a 1/8-of-N sample of the same sweep, all host threads
-  tp_stack       (N > 1) the tensor-parallel configuration: 4 QwQ-32B decoder-layer
-                 linear stacks, tensor-parallel over the N GPUs with NCCL all-reduce
+  tp_stack       the tensor-parallel configuration: 4 QwQ-32B decoder-layer linear
+                 stacks, tensor-parallel over the N GPUs (tp = 1 at N = 1) with NCCL
+                 and with the one-shot peer-memory all-reduce; layer tokens/s per M
+                 and, at N > 1, the output's distance from the tp = 1 stack
 
 Multi-GPU: one process per GPU (torchrun).  Every rank runs its own replica of
 the sweep (weak scaling; the sweep has no exchange step) and the step time is
-the max over ranks; the tensor-parallel layer stack is reported beside it.
+the max over ranks; the tensor-parallel layer stack, the configuration with an
+exchange step, is reported beside it.
 
 ``--impl reference`` times the reference's CPU implementation instead.
 """
@@ -48,7 +59,7 @@ for _p in (REPO, os.path.join(REPO, "vllm-ascend910_b200")):
 GK = 128
 SHAPES = ["qkv", "o", "gate_up", "down"]
 DECODE_MS = (1, 4, 8, 16, 32, 64)
-PREFILL_MS = (2048, 4096)
+PREFILL_MS = (1024, 2048, 4096, 8192)
 METRIC = "W4A8 GEMM HBM GB/s (decode)"
 
 
@@ -125,6 +136,9 @@ def cpu_sample(n_div=8, ms=DECODE_MS, seed=0):
         xb = syn.activation_np(M, K, seed + M)
         w = syn.weight_np(Ns, K, GK, seed + 7 + K)
         data.append((M, Ns, K, xb, w, oracle.f32_to_bf16(w.scale)))
+    # every host thread, whatever OMP_NUM_THREADS the launcher exported (torchrun sets 1)
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    oracle.set_threads(threads)
     t0 = time.perf_counter()
     tot = 0
     for M, Ns, K, xb, w, wsb in data:
@@ -135,9 +149,9 @@ def cpu_sample(n_div=8, ms=DECODE_MS, seed=0):
             oracle.gemm_kernel_order(q, oracle.bf16_to_f32(s), w.codes, w.scale, None, GK)
         tot += alg_bytes(M, Ns, K)
     dt = time.perf_counter() - t0
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     kind = "reference" if use_ref else "port"
-    desc = (f"decode sweep (24 calls) with N/{n_div} weight rows per call; "
+    desc = (f"decode sweep (24 calls) with N/{n_div} weight rows per call (the CPU GEMM's time is linear "
+            f"in N, so GB/s over the sampled bytes stands for the whole sweep); "
             + ("ReferenceMidGroupGemm (int4_cube_lab/host/gemm_ref.cpp, -O3 -fopenmp) after the C port of "
                "fakequant_lab's activation quantiser" if use_ref else "C port of the reference CPU path"))
     return tot / dt / 1e9, dt, threads, kind, desc
@@ -188,7 +202,7 @@ def l2_flush(torch, flush):
     return flush.view(torch.int64).sum()
 
 
-def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=4):
+def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=4, gk=GK):
     """Per call: the GEMM (with its stream-K fix-up) on prepared weights, the L2
     flushed by a read before each launch.  Two CUDA graphs per call -- reps x
     [flush, GEMM] and reps x [flush] -- timed with events on the replay stream;
@@ -196,7 +210,7 @@ def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=4):
     out = []
     for (shape, M) in cfgs:
         packed, scale, K, N, pw = W[shape]
-        ops.linear_quant(xs[(shape, M)], N, GK)
+        ops.linear_quant(xs[(shape, M)], N, gk)
         y = ys[(shape, M)]
         ops.linear_gemm_prepared(M, pw, y)            # workspace exists before capture
         torch.cuda.synchronize()
@@ -222,6 +236,117 @@ def time_kernels_cold(torch, ops, W, cfgs, xs, ys, flush, reps=4):
             del g
         out.append((shape, M, K, N, max(times[0] - times[1], 1e-9) / reps))
     return out
+
+
+def e2e_run(torch, ops, W, cfgs, xs, ys, steps, dev, world, step_bytes):
+    """The decode sweep end to end through the public op with host buffers.
+
+    Per step: one host->device copy of the step's 24 inputs from a pinned host
+    slab, the 24 ``ops.linear_prepared`` calls (eager, as a user makes them),
+    and one device->host copy of the 24 outputs into a pinned host slab.  Steps
+    are pipelined the way a serving loop overlaps transfers with compute: the
+    copies run on their own streams with two device slabs, so step s+1's
+    inputs travel while step s computes and step s's outputs travel back while
+    step s+1 computes.  The time runs from the first input copy's start to the
+    last output copy's end (events on the copy streams)."""
+    import torch.distributed as dist
+    bf16 = torch.bfloat16
+    xsz = [xs[c].numel() for c in cfgs]
+    ysz = [ys[c].numel() for c in cfgs]
+    xo = [0]
+    for n in xsz:
+        xo.append(xo[-1] + (n + 7) // 8 * 8)             # 16-byte aligned slices
+    yo = [0]
+    for n in ysz:
+        yo.append(yo[-1] + (n + 7) // 8 * 8)
+    xh = torch.empty(xo[-1], dtype=bf16).pin_memory()
+    for i, c in enumerate(cfgs):
+        xh[xo[i]:xo[i] + xsz[i]].copy_(xs[c].reshape(-1).cpu())
+    yh = [torch.empty(yo[-1], dtype=bf16).pin_memory() for _ in range(2)]
+    xd = [torch.empty(xo[-1], dtype=bf16, device=dev) for _ in range(2)]
+    yd = [torch.empty(yo[-1], dtype=bf16, device=dev) for _ in range(2)]
+    xv = [[xd[b][xo[i]:xo[i] + xsz[i]].view(xs[c].shape) for i, c in enumerate(cfgs)] for b in range(2)]
+    yv = [[yd[b][yo[i]:yo[i] + ysz[i]].view(ys[c].shape) for i, c in enumerate(cfgs)] for b in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = {k: [torch.cuda.Event() for _ in range(2)] for k in ("h2d", "comp", "d2h")}
+    pws = [W[c[0]][4] for c in cfgs]
+
+    def step(s):
+        b = s & 1
+        with torch.cuda.stream(h2d):
+            if s >= 2:
+                h2d.wait_event(ev["comp"][b])          # step s-2 is done reading this slab
+            xd[b].copy_(xh, non_blocking=True)
+            ev["h2d"][b].record(h2d)
+        comp.wait_event(ev["h2d"][b])
+        if s >= 2:
+            comp.wait_event(ev["d2h"][b])              # step s-2's outputs have left this slab
+        for x, pw, y in zip(xv[b], pws, yv[b]):
+            ops.linear_prepared(x, pw, out=y)
+        ev["comp"][b].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(ev["comp"][b])
+            yh[b].copy_(yd[b], non_blocking=True)
+            ev["d2h"][b].record(d2h)
+
+    for s in range(4):
+        step(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(h2d)
+    for s in range(steps):
+        step(s)
+    t1.record(d2h)
+    torch.cuda.synchronize()
+    t = t0.elapsed_time(t1) * 1e-3 / steps
+    if world > 1:
+        tt = torch.tensor([t], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    last = yh[(steps - 1) & 1]
+    same = all(torch.equal(last[yo[i]:yo[i] + ysz[i]], ys[c].reshape(-1).cpu()) for i, c in enumerate(cfgs))
+    return {"value": world * step_bytes / t / 1e9, "unit": "GB/s", "h2d_bytes_per_step": xo[-1] * 2,
+            "d2h_bytes_per_step": yo[-1] * 2, "ms_per_step": 1e3 * t, "steps": steps,
+            "matches_graph_outputs": bool(same),
+            "how": "per step one pinned H2D copy of the 24 inputs, 24 eager ops.linear_prepared calls, one "
+                   "D2H copy of the 24 outputs; copies on their own streams, double-buffered, so transfers "
+                   "of neighbouring steps overlap compute"}
+
+
+def time_config3(torch, ops, syn, dev, flush, hbm_peak, i8_peak):
+    """gate_up / down x GK {64, 128, 256} x {sym int4, asym
+    uint4 + zero point}: GEMM GB/s at M = 16 and int8 TOP/s at M = 4096 (the
+    cold-L2 graph-difference timing of the roofline line)."""
+    from w4a8_b200.synthetic import QWQ_SHAPES
+    rows = []
+    for shape in ("gate_up", "down"):
+        K, N = QWQ_SHAPES[shape]
+        for gk in (64, 128, 256):
+            for asym in (False, True):
+                codes, scale, zero = syn.weight_torch(N, K, gk, 300 + gk, dev, asym=asym)
+                packed = ops.pack_int4_grouped(codes, gk)
+                del codes
+                pw = ops.prepare_weights(packed, scale, zero, K, gk)
+                Wc = {shape: (packed, scale, K, N, pw)}
+                for M in (16, 4096):
+                    x = syn.activation_torch(M, K, 310 + M, dev)
+                    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+                    (_, _, _, _, t), = time_kernels_cold(torch, ops, Wc, [(shape, M)], {(shape, M): x},
+                                                         {(shape, M): y}, flush, reps=2, gk=gk)
+                    by = alg_bytes(M, N, K, gk, 4, asym)
+                    r = {"shape": shape, "gk": gk, "weights": "asym" if asym else "sym", "M": M,
+                         "us": round(t * 1e6, 2)}
+                    if M == 16:
+                        r.update(GBps=round(by / t / 1e9, 1), frac_hbm=round(by / t / 1e9 / hbm_peak, 3))
+                    else:
+                        tops = 2 * M * N * K / t / 1e12
+                        r.update(TOPS=round(tops, 1), frac_int8=round(tops / i8_peak, 3) if i8_peak else None)
+                    rows.append(r)
+                del Wc, pw, packed
+    return rows
 
 
 def int8_peak_tops(torch, dev):
@@ -306,37 +431,7 @@ def run_gpu(args, rank, world, local_rank):
     status = ops.workspace_status(dev)
 
     # ---- end to end through the public op, host buffers ----
-    xh = {k: v.cpu().pin_memory() for k, v in xs.items()}
-    yh = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in ys.items()}
-    xd = {k: torch.empty_like(v) for k, v in xs.items()}
-    h2d = sum(v.numel() * 2 for v in xh.values())
-    d2h = sum(v.numel() * 2 for v in yh.values())
-
-    def e2e_step():
-        for (s, M) in cfgs:
-            xd[(s, M)].copy_(xh[(s, M)], non_blocking=True)
-            y = ops.linear_prepared(xd[(s, M)], W[s][4])
-            yh[(s, M)].copy_(y, non_blocking=True)
-
-    n_e2e = max(3, min(args.steps, 20))
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0.record()
-    for _ in range(n_e2e):
-        e2e_step()
-    a1.record()
-    torch.cuda.synchronize()
-    t_e2e = a0.elapsed_time(a1) * 1e-3 / n_e2e
-    if world > 1:
-        t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_e2e = float(t.item())
-    e2e = {"value": world * step_bytes / t_e2e / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "ms_per_step": 1e3 * t_e2e, "steps": n_e2e}
+    e2e = e2e_run(torch, ops, W, cfgs, xs, ys, max(3, min(args.steps, 20)), dev, world, step_bytes)
 
     # ---- dominant kernel alone (GEMM), cold L2, events per launch ----
     flush = torch.ones(512 << 20, dtype=torch.uint8, device=dev)
@@ -368,17 +463,18 @@ def run_gpu(args, rank, world, local_rank):
         pre.append({"shape": s, "M": M, "us": round(t * 1e6, 1), "TOPS": round(2 * M * N * K / t / 1e12, 1)})
     del big
     i8_peak = int8_peak_tops(torch, dev)
-    pre_tops = sum(2 * M * N * K for (_, M, K, N, _) in pk) / sum(t for *_, t in pk) / 1e12
+    pk2 = [r for r in pk if r[1] >= 2048]
+    pre_tops = sum(2 * M * N * K for (_, M, K, N, _) in pk2) / sum(t for *_, t in pk2) / 1e12
+    cfg3 = None if args.no_config3 else time_config3(torch, ops, syn, dev, flush, hbm_peak, i8_peak)
+    status = status or ops.workspace_status(dev)
     clocks = sampler.stop()
 
-    # ---- tensor-parallel layer stack (config 4) ----
+    # ---- tensor-parallel layer stack (config 4), tp = N ----
     tp = None
-    if world > 1 or args.tp_stack:
+    if not args.no_tp_stack:
         from w4a8_b200 import tp as tpmod
         tp = tpmod.bench_stack(world, rank, dev, ms=(16, 256, 4096), layers=4, iters=max(3, min(args.steps, 20)),
-                               hbm_gbs=hbm_peak, i8_tops=i8_peak,
-                               # the one-shot all-reduce is verified on 2 and 4 GPUs
-                               allreduces=("nccl", "custom") if 1 < world <= 4 else ("nccl",))
+                               hbm_gbs=hbm_peak, i8_tops=i8_peak, allreduces=("nccl", "custom"))
 
     if rank != 0:
         return
@@ -399,11 +495,15 @@ def run_gpu(args, rank, world, local_rank):
                    "calls_per_step": len(cfgs), "alg_bytes_per_step": step_bytes,
                    "l2": "inputs larger than L2: 244 MB of weights per step, shapes interleaved",
                    "timing": "CUDA graph of the step, events on the replay stream, max over ranks",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "reference_arm": "the reference's C++ CPU GEMM on all host cores of the box (whatever N), "
+                                    "on an N/8 sample of each call's weight rows; its time is linear in N"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
                      "kernel": "w4a8_gemm_kernel + its stream-K fix-up, prepared weights, L2 flushed by a "
-                               "512 MB read before each launch; graph [flush, GEMM] minus graph [flush]",
+                               "512 MB read before each launch; graph [flush, GEMM] minus graph [flush]; "
+                               "timed alone and cold, so each launch pays the pipeline fill the chained "
+                               "step overlaps with the previous call",
                      "traffic_source": "profiles/gemm_decode_traffic.json (ncu, the same 24 calls, per launch)",
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src},
         "e2e": e2e,
@@ -421,6 +521,8 @@ def run_gpu(args, rank, world, local_rank):
     }
     if tp is not None:
         line["tp_stack"] = tp
+    if cfg3 is not None:
+        line["config3"] = cfg3
     print(json.dumps(line))
 
 
@@ -489,7 +591,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--tp-stack", action="store_true", help="also run the TP layer stack at N=1")
+    ap.add_argument("--no-tp-stack", action="store_true", help="skip the tensor-parallel layer stack")
+    ap.add_argument("--no-config3", action="store_true", help="skip the group-size / asymmetry lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", default=None, help="SHAPE:M, e.g. qkv:16 (ncu target)")
     ap.add_argument("--profile-sweep", action="store_true", help="each decode call once, cold (ncu target)")

@@ -62,8 +62,15 @@ def lib() -> ctypes.CDLL:
         L.orc_gemm_kernel_order.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _p]
         L.orc_gemm_f64.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _p]
         L.orc_f32_to_bf16_array.argtypes = [_p, _i64, _p]
+        L.orc_set_threads.argtypes = [_i32]
         _LIB = L
     return _LIB
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads for the oracle's and the reference C++ GEMM's loops (one
+    process-wide setting; independent of OMP_NUM_THREADS in the environment)."""
+    lib().orc_set_threads(int(n))
 
 
 def ref_available() -> bool:

@@ -302,3 +302,19 @@ ORC_API void orc_f32_to_bf16_array(const float* in, int64_t n, uint16_t* out)
 {
     for (int64_t i = 0; i < n; ++i) out[i] = orc_f32_to_bf16(in[i]);
 }
+
+/* Threads of the OpenMP loops above (the process-wide setting: the reference
+ * C++ GEMM linked into the same process shares it).  A launcher that exports
+ * OMP_NUM_THREADS=1 to each rank (torchrun) would otherwise leave the CPU
+ * baseline on one core. */
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+ORC_API void orc_set_threads(int32_t n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

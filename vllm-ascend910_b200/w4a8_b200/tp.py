@@ -266,19 +266,26 @@ def custom_allreduce(group=None, max_bytes: Optional[int] = None):
 
 def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4, iters: int = 10,
                 hbm_gbs: float = 6556.5, i8_tops: Optional[float] = None,
-                allreduces: Sequence[str] = ("nccl",)) -> Dict:
+                allreduces: Sequence[str] = ("nccl",), parity: bool = True) -> Dict:
     """Time `layers` sharded layers at each M on `world` GPUs (one rank each).
 
     The step is captured in a CUDA graph (the all-reduces included); the time is
     the max over ranks of CUDA-event time per forward.  Returns tokens/s (M per
     forward) and layer-tokens/s (M x layers per forward) with the roofline
     fraction, per all-reduce (``nccl``, or ``custom``: the one-shot kernel for
-    small messages, NCCL for the rest)."""
+    small messages, NCCL for the rest).
+
+    With ``parity`` and world > 1, rank 0 also runs the unsharded stack (tp = 1,
+    the same seeded weights and inputs) and reports, per all-reduce and M, how
+    far the tensor-parallel output is from it (the stack bound: max rel <= 3e-2,
+    cosine >= 0.9995) and whether every rank holds the same bits."""
     d = QWQ
     Ls = build_layers(layers, rank, world, dev, d, prepare=True)
     out = {"tp": world, "layers": layers, "dims": dataclasses.asdict(d),
-           "note": "attention replaced by the rank's q section of the QKV output"}
-    for mode in allreduces:
+           "note": "attention replaced by the rank's q section of the QKV output; the down projection "
+                   "applies silu(gate)*up in its activation quantiser"}
+    outs = {}
+    for mode in allreduces if world > 1 else ("none",):
         car = None
         if world == 1:
             ar = (lambda t: None)
@@ -287,33 +294,70 @@ def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4,
             ar = car
         else:
             ar = nccl_allreduce()
-        key = "per_M" if mode == "nccl" else f"per_M_{mode}"
-        out[key] = _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops)
+        key = "per_M" if mode in ("nccl", "none") else f"per_M_{mode}"
+        out[key], outs[mode] = _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops)
         if car is not None:
             car.check()
             car.close()
+    del Ls
+    if parity and world > 1:
+        out["tp_parity"] = _stack_parity(world, rank, dev, layers, ms, d, outs)
     return out
 
 
-def _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops) -> List[Dict]:
+def _stack_parity(world, rank, dev, layers, ms, d, outs) -> Dict:
+    import torch.distributed as dist
+    res = {"bound": {"max_rel": 3e-2, "cos": 0.9995}, "per": []}
+    ref = {}
+    if rank == 0:
+        L1 = build_layers(layers, 0, 1, dev, d, prepare=True)
+        for M in ms:
+            ref[M] = stack_forward(_stack_input(M, d, dev), L1, 1, cuda_linear, lambda t: None, d,
+                                   cuda_swiglu_linear).float()
+        del L1
+    ok_all = True
+    for mode, per_m in outs.items():
+        for M, y in per_m.items():
+            # every rank's bits: a checksum of the bf16 words, gathered
+            h = y.contiguous().view(torch.int16).to(torch.int64).sum().reshape(1)
+            hs = [torch.zeros_like(h) for _ in range(world)]
+            dist.all_gather(hs, h)
+            same = all(int(x.item()) == int(hs[0].item()) for x in hs)
+            if rank == 0:
+                yf, r = y.float(), ref[M]
+                err = float((yf - r).abs().max() / r.abs().max())
+                cos = float((yf * r).sum() / (yf.norm() * r.norm()))
+                ok = err <= 3e-2 and cos >= 0.9995 and same
+                ok_all &= ok
+                res["per"].append({"allreduce": mode, "M": M, "max_rel": err, "cos": cos,
+                                   "ranks_identical": same, "ok": ok})
+    res["ok"] = ok_all
+    return res
+
+
+def _stack_input(M: int, d: Dims, dev) -> torch.Tensor:
+    gen = torch.Generator(device=dev).manual_seed(99 + M)
+    return torch.randn(M, d.hidden, generator=gen, device=dev).to(torch.bfloat16)
+
+
+def _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops):
     import torch.distributed as dist
     layers = len(Ls)
-    res = []
+    res, outs = [], {}
     for M in ms:
-        gen = torch.Generator(device=dev).manual_seed(99 + M)
-        h0 = torch.randn(M, d.hidden, generator=gen, device=dev).to(torch.bfloat16)
+        h0 = _stack_input(M, d, dev)
 
         def fwd():
-            return stack_forward(h0, Ls, world, cuda_linear, ar, d)
+            return stack_forward(h0, Ls, world, cuda_linear, ar, d, cuda_swiglu_linear)
 
         for _ in range(2):
             fwd()
         torch.cuda.synchronize()
-        graph = None
+        graph, y = None, None
         try:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                fwd()
+                y = fwd()
         except Exception:
             graph = None
         run = graph.replay if graph is not None else fwd
@@ -333,9 +377,10 @@ def _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops) -> List[Dict
             tt = torch.tensor([t], device=dev, dtype=torch.float64)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             t = float(tt.item())
+        outs[M] = (y if graph is not None else fwd()).clone()
         roof = _roofline_seconds(Ls, M, hbm_gbs, i8_tops)
         res.append({"M": M, "ms_per_forward": 1e3 * t, "tokens_per_s": M / t,
                     "layer_tokens_per_s": M * layers / t, "roofline_frac": roof / t,
                     "graph": graph is not None})
         del graph
-    return res
+    return res, outs
