@@ -231,6 +231,14 @@ W4A8_API int w4a8_last_cuda_error(void);
 /* Library build: returns the sm architecture it was compiled for (100). */
 W4A8_API int w4a8_build_arch(void);
 
+/* ---- options (process-wide; no counterpart in the reference) ----
+ * W4A8_OPT_NO_FUSED_QUANT: every linear call runs the standalone quantiser
+ * kernel before the GEMM.  By default a call with M <= 16, group size <= 256
+ * and 16-byte aligned activation rows quantises inside the GEMM instead (one
+ * launch fewer; the same bits).  Returns the previous flags. */
+#define W4A8_OPT_NO_FUSED_QUANT 1
+W4A8_API int w4a8_set_options(int32_t flags);
+
 #ifdef __cplusplus
 }
 #endif

@@ -257,10 +257,80 @@ struct Weights {
     int32_t ws_dtype;
 };
 
-int run_gemm(const Plan& pl, const Weights& w, void* out, int64_t ldy, bool partials, uint8_t* ws, cudaStream_t st)
+// Tensor maps over activations (fused quantisation), keyed by (pointer, shape,
+// stride, device): a serving loop reuses a few activation buffers, so most
+// calls find their map here instead of encoding it again.
+struct XMapKey {
+    const void* x;
+    int64_t M, K, ldx;
+    int dev, pad;
+    bool operator==(const XMapKey& o) const { return std::memcmp(this, &o, sizeof(XMapKey)) == 0; }
+};
+
+struct XMapEntry {
+    XMapKey key;
+    CUtensorMap map;
+    uint64_t stamp;
+    bool used;
+};
+
+constexpr int kXMapCache = 256;
+XMapEntry g_xmaps[kXMapCache];
+uint64_t g_xmap_clock = 0;
+
+bool cached_x_map(const void* x, int64_t M, int64_t K, int64_t ldx, CUtensorMap* out)
+{
+    XMapKey k;
+    std::memset(&k, 0, sizeof(k));
+    k.x = x;
+    k.M = M;
+    k.K = K;
+    k.ldx = ldx;
+    cudaGetDevice(&k.dev);
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    int victim = 0;
+    XMapEntry* hit = nullptr;
+    for (int i = 0; i < kXMapCache && !hit; ++i) {
+        if (g_xmaps[i].used && g_xmaps[i].key == k) hit = &g_xmaps[i];
+        else if (g_xmaps[victim].used && (!g_xmaps[i].used || g_xmaps[i].stamp < g_xmaps[victim].stamp)) victim = i;
+    }
+    if (!hit) {
+        XMapEntry& e = g_xmaps[victim];
+        e.used = false;
+        // box: 256 positions x 16 rows of bf16; rows >= M and positions >= K read as zero
+        if (!encode_2d(&e.map, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
+                       static_cast<uint64_t>(ldx) * 2, 256, 16, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+        e.key = k;
+        e.used = true;
+        hit = &e;
+    }
+    hit->stamp = ++g_xmap_clock;
+    std::memcpy(out, &hit->map, sizeof(CUtensorMap));
+    return true;
+}
+
+// Library options (w4a8_set_options).
+int g_options = 0;
+
+// Whether a linear call quantises its activation inside the GEMM: one 16-token
+// tile (M <= 16), GK <= 256, and an activation the 2-D tensor copies can read
+// (16-byte aligned rows).  Everything else runs the standalone quantiser first.
+bool fused_quant_ok(const Plan& pl, const void* x, int64_t ldx, bool swiglu)
+{
+    return !(g_options & W4A8_OPT_NO_FUSED_QUANT) && !swiglu && pl.tt == 16 && pl.n_tt == 1 && pl.gk <= 256 &&
+           aligned(x, 16) && ldx % 8 == 0;
+}
+
+int run_gemm(const Plan& pl, const Weights& w, void* out, int64_t ldy, bool partials, uint8_t* ws, cudaStream_t st,
+             const void* fq_x = nullptr, int64_t fq_ldx = 0)
 {
     GemmParams g;
     std::memset(&g, 0, sizeof(g));
+    if (fq_x) {
+        if (get_encoder() != W4A8_OK) return fail_cuda(cudaErrorNotSupported);
+        if (!cached_x_map(fq_x, pl.M, pl.K, fq_ldx, &g.tm_x)) return W4A8_ERR_INVALID;
+    }
     const bool asym = w.prepared ? w.has_zero : (w.w_zero != nullptr);
     if (w.prepared) {
         const PreparedLayout L = prepared_layout(pl.N, pl.G, pl.kb_total, w.ws_dtype == W4A8_DTYPE_F32 ? 4 : 2, asym);
@@ -292,6 +362,7 @@ int run_gemm(const Plan& pl, const Weights& w, void* out, int64_t ldy, bool part
     c.asym = asym;
     c.ws_bf16 = w.ws_dtype != W4A8_DTYPE_F32;
     c.partials = partials;
+    c.fq = fq_x != nullptr;
     cudaError_t e = launch_gemm(g, c, pl.grid, st, true);
     if (e != cudaSuccess) return fail_cuda(e);
     if (!partials && pl.split) e = launch_splitk_reduce(g, pl.tt, pl.grid, st);
@@ -384,6 +455,19 @@ int fixed_scratch(cudaStream_t st, uint8_t** out)
     return W4A8_OK;
 }
 
+// The launches of one linear call on a planned workspace: the GEMM with the
+// quantiser fused in when the call allows it, else the standalone quantiser
+// and then the GEMM.  Both give the same bits (same codes, scales and
+// accumulation order).
+int run_linear(const Plan& pl, const void* x, int64_t ldx, const Weights& w, void* y, int64_t ldy, uint8_t* ws,
+               cudaStream_t st, bool swiglu)
+{
+    if (fused_quant_ok(pl, x, ldx, swiglu)) return run_gemm(pl, w, y, ldy, false, ws, st, x, ldx);
+    const int rc = run_quant_kernel_layout(pl, x, ldx, ws, st, swiglu);
+    if (rc != W4A8_OK) return rc;
+    return run_gemm(pl, w, y, ldy, false, ws, st);
+}
+
 int linear_impl(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk, const void* w_packed,
                 const void* w_scale, int32_t ws_dtype, const void* w_zero, void* y, int64_t ldy, void* workspace,
                 size_t workspace_bytes, void* stream, bool swiglu)
@@ -398,11 +482,9 @@ int linear_impl(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int
     if ((rc = device_info(&sms)) != W4A8_OK) return rc;
     const Plan pl = make_plan(M, N, K, gk, sms);
     if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st, swiglu)) != W4A8_OK) return rc;
     const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
-    return run_gemm(pl, w, y, ldy, false, ws, st);
+    return run_linear(pl, x, ldx, w, y, ldy, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream),
+                      swiglu);
 }
 
 int linear_prepared_impl(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
@@ -420,11 +502,9 @@ int linear_prepared_impl(const void* x, int64_t M, int64_t K, int64_t ldx, int64
     if ((rc = device_info(&sms)) != W4A8_OK) return rc;
     const Plan pl = make_plan(M, N, K, gk, sms);
     if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st, swiglu)) != W4A8_OK) return rc;
     const Weights w{nullptr, nullptr, nullptr, static_cast<const uint8_t*>(prepared), has_zero != 0, ws_dtype};
-    return run_gemm(pl, w, y, ldy, false, ws, st);
+    return run_linear(pl, x, ldx, w, y, ldy, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream),
+                      swiglu);
 }
 
 }  // namespace
@@ -518,9 +598,8 @@ int w4a8_linear_fixed_scratch(const void* x, int64_t M, int64_t K, int64_t ldx, 
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     uint8_t* ws = nullptr;
     if ((rc = fixed_scratch(st, &ws)) != W4A8_OK) return rc;
-    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st)) != W4A8_OK) return rc;
     const Weights w{w_packed, w_scale, w_zero, nullptr, false, ws_dtype};
-    return run_gemm(pl, w, y, ldy, false, ws, st);
+    return run_linear(pl, x, ldx, w, y, ldy, ws, st, false);
 }
 
 int w4a8_fixed_scratch_status(int32_t reset, void* stream)
@@ -750,5 +829,12 @@ const char* w4a8_status_string(int s)
 int w4a8_last_cuda_error(void) { return g_last_cuda; }
 
 int w4a8_build_arch(void) { return 100; }
+
+int w4a8_set_options(int32_t flags)
+{
+    const int old = g_options;
+    g_options = flags;
+    return old;
+}
 
 }  // extern "C"

@@ -336,4 +336,80 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f)
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (the tensor core's operand reads, bulk copies) before a barrier
+// arrival hands the buffer over.
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- activation quantisation
+// The reference's rule (fakequant_lab/quant.py:89-141), per (token, K-group):
+//   s = bf16_rne(amax / 127) (IEEE division), bf16 tiny when that is 0
+//   q = clamp(rint(x / s), -128, 127)        (IEEE division, half-even)
+
+// Scale bits from the group's amax (quant.py:102-105).
+__device__ __forceinline__ uint16_t act_scale_bits(float amax)
+{
+    uint16_t sb = f32_to_bf16_bits(__fdiv_rn(amax, 127.0f));
+    if ((sb & 0x7FFFu) == 0) sb = 0x0080u;
+    return sb;
+}
+
+// One code with the true division.
+__device__ __forceinline__ int quant_exact(float xv, float s)
+{
+    float r = rintf(__fdiv_rn(xv, s));
+    r = fminf(fmaxf(r, -128.0f), 127.0f);
+    return static_cast<int>(r);
+}
+
+// One code without a division: y = x * (1/s), and the true division only
+// when y is within 2^-11 of a half-integer.  For a normal s, x / s (x, s bf16)
+// is either a half-integer or at least 1/1020 from every half-integer, while
+// |y - x / s| <= 2^-16, so rint(y) equals rint(x / s) outside that window and
+// every tie falls inside it; |x / s| < 127.5 because s = bf16(amax / 127), so
+// the clamp cannot bind.  `rcp` = __frcp_rn(s); callers take quant_exact for
+// the whole group when s is a bf16 subnormal (act_scale_fast false).
+__device__ __forceinline__ int quant_fast(float xv, float s, float rcp)
+{
+    const float y = __fmul_rn(xv, rcp);
+    const float n = rintf(y);
+    if (fabsf(__fsub_rn(y, n)) > 0.49951171875f) return quant_exact(xv, s);
+    return static_cast<int>(n);
+}
+
+__device__ __forceinline__ bool act_scale_fast(uint16_t sb) { return (sb & 0x7F80u) != 0; }
+
+// 8 codes k0..k7 -> two words in the GEMM's operand order: k0 k2 k4 k6 | k1 k3 k5 k7.
+__device__ __forceinline__ uint2 pack_operand_order(const int (&q)[8])
+{
+    const uint32_t lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) |
+                        (static_cast<uint32_t>(q[6] & 0xFF) << 24);
+    const uint32_t hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) |
+                        (static_cast<uint32_t>(q[7] & 0xFF) << 24);
+    return make_uint2(lo, hi);
+}
+
+// The stack's activation on one element: bf16(silu(g) * u) with
+// silu(g) = g / (1 + exp(-g)) in fp32, as the reference computes it in torch
+// (F.silu(g) * u, npu_ops/python/bench_decode_layer.py:81) before quantising.
+__device__ __forceinline__ float swiglu_bf16(float g, float u)
+{
+    const float a = __fmul_rn(__fdiv_rn(g, 1.0f + expf(-g)), u);
+    return bf16_bits_to_f32(f32_to_bf16_bits(a));
+}
+
+// 8 bf16 values (one 16-byte word) -> fp32.
+__device__ __forceinline__ void unpack8_bf16(uint4 v, float (&x)[8])
+{
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        x[2 * i] = __uint_as_float(w[i] << 16);
+        x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
 }  // namespace w4a8

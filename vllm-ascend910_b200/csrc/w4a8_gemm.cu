@@ -46,13 +46,20 @@ constexpr int kBarBytes = 1024;
 
 // wait-site ids for the status word
 enum { kWProdEmpty = 1, kWActEmpty, kWProdSlot, kWConvFull, kWConvAEmpty, kWMmaFull, kWMmaAFull, kWMmaAccEmpty,
-       kWEpiSlot, kWEpiAccFull, kWDrain };
+       kWEpiSlot, kWEpiAccFull, kWDrain, kWQuantSlot, kWQuantX, kWQuantAEmpty };
 
-template <int TT_, int GK_, bool ASYM_>
+// FQ_: the activation is quantised inside the GEMM.  Warp 3 then streams the
+// bf16 activation (2-D tensor copies into a staging ring) instead of codes,
+// and four more warps quantise each stage straight into the MMA operand
+// buffer and the unit's scale slot.  Built for one 16-token tile (decode),
+// GK <= 256.
+template <int TT_, int GK_, bool ASYM_, bool FQ_ = false>
 struct Cfg {
     static constexpr int TT = TT_;
     static constexpr int GK = GK_;
     static constexpr bool ASYM = ASYM_;
+    static constexpr bool FQ = FQ_;
+    static_assert(!FQ || (TT == 16 && GK <= 256), "fused quantisation: 16-token tiles, GK <= 256");
     // Pipeline granularity.  Every hand-over between warps costs a few
     // hundred cycles of mbarrier latency, so small token tiles move two
     // k-blocks (32 KB of int4 weights) per stage.
@@ -64,7 +71,9 @@ struct Cfg {
     static constexpr int E = TT <= 16 ? 1 : 2;               // epilogue warpgroups
     static constexpr int NC = TT / E;                        // accumulator columns per thread
     static constexpr int NCH = NC / 16;                      // 16-column TMEM chunks per thread
-    static constexpr int THREADS = (kNumPreWarps + 4 * E) * 32;
+    static constexpr int NQW = FQ ? 4 : 0;                   // quantiser warps
+    static constexpr int QWARP0 = kNumPreWarps + 4 * E;      // first quantiser warp
+    static constexpr int THREADS = (kNumPreWarps + 4 * E + NQW) * 32;
     // TMEM: NA A buffers of KS x 64 columns (the stage's int8 weights), the
     // rest for accumulator slots of CG groups x TT columns.
     static constexpr int ABUF = KS * 64;
@@ -88,7 +97,10 @@ struct Cfg {
     //   S_W zero-point rows   (asymmetric) the unit's GPU x 128 bf16, loaded with its first stage
     //   DS scale slots        one unit's [GPU][128] weight scales (sized for fp32) and
     //                         [GPU][TT] activation scales, filled by the activation
-    //                         producer, released by the epilogue
+    //                         producer (FQ: weight scales by warp 3, activation
+    //                         scales by the quantiser warps), released by the epilogue
+    //   XS x stages           (FQ) KS boxes of TT rows x 256 bf16, filled by warp 3,
+    //                         released by the quantiser warps
     //   barriers
     static constexpr int A_TILE = TT * 256;
     static constexpr int A_STAGE = KS * A_TILE;
@@ -98,14 +110,19 @@ struct Cfg {
     static constexpr int SL_WS = GPU * 128 * 4;
     static constexpr int SL_AS = GPU * TT * 4;
     static constexpr int SLOT = r128(SL_WS) + r128(SL_AS);
-    static constexpr int DS = 8;
-    static constexpr int S_A = TT <= 16 ? 4 : (TT <= 32 ? 2 : (TT <= 64 ? 4 : 3));
-    static constexpr int S_W_FIT = (kSmemBudget - kBarBytes - DS * SLOT - S_A * A_STAGE) / (W_STAGE + WZ_SLOT);
+    static constexpr int DS = FQ ? 6 : 8;
+    static constexpr int S_A = FQ ? 2 : (TT <= 16 ? 4 : (TT <= 32 ? 2 : (TT <= 64 ? 4 : 3)));
+    static constexpr int X_BOX = TT * 512;                   // one 2-D copy: TT rows x 256 bf16
+    static constexpr int X_STAGE = FQ ? KS * X_BOX : 0;
+    static constexpr int XS = FQ ? 2 : 0;
+    static constexpr int S_W_FIT = (kSmemBudget - kBarBytes - DS * SLOT - S_A * A_STAGE - XS * X_STAGE - (FQ ? 1024 : 0)) /
+                                   (W_STAGE + WZ_SLOT);
     static constexpr int S_W = S_W_FIT > 16 ? 16 : S_W_FIT;
     static constexpr int OFF_A = S_W * W_STAGE;
     static constexpr int OFF_WZ = OFF_A + S_A * A_STAGE;
     static constexpr int OFF_SL = OFF_WZ + S_W * WZ_SLOT;
-    static constexpr int BAR_OFF = OFF_SL + DS * SLOT;
+    static constexpr int OFF_X = (OFF_SL + DS * SLOT + 1023) / 1024 * 1024;
+    static constexpr int BAR_OFF = FQ ? OFF_X + XS * X_STAGE : OFF_SL + DS * SLOT;
     static constexpr int SMEM = BAR_OFF + kBarBytes + 1024;  // + alignment slack
     static constexpr int TMEM_COLS = 512;
     static_assert(S_W >= 3 && S_A >= 2, "pipeline too shallow");
@@ -115,6 +132,7 @@ struct Cfg {
     static_assert(TOTCH % BCH == 0, "slots split into whole batches");
     static_assert(OFF_A % 1024 == 0 && OFF_WZ % 1024 == 0, "tile alignment");
     static_assert(SMEM <= 227 * 1024, "shared memory");
+    static_assert(!FQ || (S_A >= 2 && XS >= 2), "fused quantisation rings");
     // Register split for the 64/128-token tiles (2 + E warpgroups): producers +
     // MMA issuers and converters give registers to the epilogue warpgroups,
     // which hold NC fp32 accumulators per thread.  The sum stays within the
@@ -122,6 +140,7 @@ struct Cfg {
     // the host also checks it against the compiled register count.
     static constexpr int NWG = 2 + E;
     static constexpr bool SPLIT_REGS = TT >= 64;
+    static_assert(!(FQ && SPLIT_REGS), "the register split does not count quantiser warps");
     static constexpr int LAUNCH_REGS = (65536 / THREADS) / 8 * 8;
     static constexpr int REGS_PRE = 56;
     static constexpr int REGS_CONV = E <= 2 ? 80 : 72;
@@ -137,6 +156,7 @@ struct Bars {
     uint64_t tfull[4], tempty[4];       // converted weights in TMEM
     uint64_t accfull[8], accempty[8];   // accumulator slots
     uint64_t sfull[8], sempty[8];       // scale slots
+    uint64_t xfull[2], xempty[2];       // bf16 activation stages (fused quantisation)
     uint64_t drain[2];
     uint32_t tmem_base;
     int abort;
@@ -283,11 +303,12 @@ __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, 
 // PART: the debug mode that writes each group's exact int32 partials instead
 // of y.  It is a separate instantiation (16-token tiles only) so the product
 // epilogue carries no call and no second output path.
-template <int TT, int GK, bool ASYM, bool PART>
-__global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
+template <int TT, int GK, bool ASYM, bool PART, bool FQ>
+__global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
     w4a8_gemm_kernel(const __grid_constant__ GemmParams p, const int ws_bf16)
 {
-    using C = Cfg<TT, GK, ASYM>;
+    using C = Cfg<TT, GK, ASYM, FQ>;
+    static_assert(!(PART && FQ), "the partials mode reads codes from the standalone quantiser");
     extern __shared__ uint8_t smem_raw[];
     // Align by an offset from the __shared__ array itself: a pointer rebuilt from
     // an integer loses the address space, and every read through it would be a
@@ -307,6 +328,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
     auto w_zero = [&](int s) { return smem + C::OFF_WZ + s * C::WZ_SLOT; };
     auto slot_ws = [&](int s) { return smem + C::OFF_SL + s * C::SLOT; };
     auto slot_as = [&](int s) { return reinterpret_cast<float*>(slot_ws(s) + C::r128(C::SL_WS)); };
+    auto x_stage = [&](int s) { return smem + C::OFF_X + s * C::X_STAGE; };
 
     // ---------------------------------------------------------------- setup
     if (threadIdx.x == 0) {
@@ -315,8 +337,12 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             mbar_init(&bars->wempty[i], 4);                 // 4 converter warps
         }
         for (int i = 0; i < C::S_A; ++i) {
-            mbar_init(&bars->afull[i], 1);                  // activation producer (+ bytes)
+            mbar_init(&bars->afull[i], C::FQ ? C::NQW : 1); // activation producer (+ bytes) / quantiser warps
             mbar_init(&bars->aempty[i], 1);                 // the owning issuer's commit
+        }
+        for (int i = 0; i < C::XS; ++i) {
+            mbar_init(&bars->xfull[i], 1);                  // warp 3 (+ bytes)
+            mbar_init(&bars->xempty[i], C::NQW);            // quantiser warps
         }
         for (int i = 0; i < C::NA; ++i) {
             mbar_init(&bars->tfull[i], 4);
@@ -327,7 +353,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
             mbar_init(&bars->accempty[i], 4 * C::E);
         }
         for (int i = 0; i < C::DS; ++i) {
-            mbar_init(&bars->sfull[i], 1);                  // activation producer (+ bytes)
+            mbar_init(&bars->sfull[i], 1 + C::NQW);         // activation producer (+ bytes), quantiser warps
             mbar_init(&bars->sempty[i], 4 * C::E);          // epilogue warps
         }
         mbar_init(&bars->drain[0], 1);
@@ -366,14 +392,16 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 if (C::ASYM) tma_prefetch_desc(&p.tm_wz);
             }
             if (!wside && !prepared && !PART) tma_prefetch_desc(&p.tm_ws);
+            if (!wside && C::FQ) tma_prefetch_desc(&p.tm_x);
             if (!wside) pdl_wait();
             // Weights stream once when there is one token tile (decode): evict
             // them first.  With several token tiles a CTA re-reads its weight
             // tile once per token tile, so they must stay in L2.
             const uint64_t pol = (wside && p.n_tt == 1) ? policy_evict_first() : policy_evict_last();
-            const int ns = wside ? C::S_W : C::S_A;
-            uint64_t* fullb = wside ? bars->wfull : bars->afull;
-            uint64_t* emptyb = wside ? bars->wempty : bars->aempty;
+            // warp 3's stage ring: activation codes, or (FQ) bf16 activation boxes
+            const int ns = wside ? C::S_W : (C::FQ ? C::XS : C::S_A);
+            uint64_t* fullb = wside ? bars->wfull : (C::FQ ? bars->xfull : bars->afull);
+            uint64_t* emptyb = wside ? bars->wempty : (C::FQ ? bars->xempty : bars->aempty);
             int stage = 0, issued = 0, slot = 0, sissued = 0;
             uint32_t ph = 0, slph = 0;
             bool ok = true;
@@ -389,15 +417,17 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                     } else {
                         const uint32_t ng = static_cast<uint32_t>(g1 - g0);
                         const uint32_t wsb = prepared ? ng * 128u * ws_elt : C::GPU * 128u * ws_elt;
-                        const uint32_t asb = ng * static_cast<uint32_t>(C::TT * 4);
+                        // (FQ: the quantiser warps write the activation scales)
+                        const uint32_t asb = C::FQ ? 0u : ng * static_cast<uint32_t>(C::TT * 4);
                         mbar_arrive_expect_tx(&bars->sfull[slot], wsb + asb);
                         if (prepared)
                             bulk_load(slot_ws(slot), p.ws_tiles + (static_cast<int64_t>(un.wt) * p.G + g0) * 128 * ws_elt,
                                       wsb, &bars->sfull[slot], pol);
                         else
                             tma_load_2d(slot_ws(slot), &p.tm_ws, &bars->sfull[slot], un.wt * 128, g0);
-                        bulk_load(slot_as(slot), p.as_tiles + (static_cast<int64_t>(un.tt) * p.G + g0) * C::TT, asb,
-                                  &bars->sfull[slot], pol);
+                        if (!C::FQ)
+                            bulk_load(slot_as(slot), p.as_tiles + (static_cast<int64_t>(un.tt) * p.G + g0) * C::TT, asb,
+                                      &bars->sfull[slot], pol);
                     }
                     ++sissued;
                     if (++slot == C::DS) { slot = 0; slph ^= 1; }
@@ -427,6 +457,12 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                             else
                                 tma_load_2d(w_zero(stage), &p.tm_wz, &fullb[stage], un.wt * 128, g0);
                         }
+                    } else if (C::FQ) {
+                        // bf16 x: one TT-row x 256-position box per k-block (zeros past M and K)
+                        mbar_arrive_expect_tx(&fullb[stage], static_cast<uint32_t>(kn * C::X_BOX));
+                        for (int j = 0; j < kn; ++j)
+                            tma_load_2d_hint(x_stage(stage) + j * C::X_BOX, &p.tm_x, &fullb[stage], (kbs + j) * 256,
+                                             un.tt * C::TT, pol);
                     } else {
                         mbar_arrive_expect_tx(&fullb[stage], static_cast<uint32_t>(kn * C::A_TILE));
                         bulk_load(a_stage(stage), p.a_tiles + (static_cast<int64_t>(un.tt) * p.kb_total + kbs) * C::A_TILE,
@@ -642,6 +678,86 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM>::THREADS, 1)
                 if (++ab == C::NA) { ab = 0; abph ^= 1; }
                 if (++stage == C::S_W) { stage = 0; sph ^= 1; }
             }
+        }
+    } else if (C::FQ && warp >= C::QWARP0) {
+        // ============================================================ quantiser (FQ)
+        // Per stage: the bf16 boxes warp 3 staged -> per (row, group) amax over
+        // the group's lanes -> scale (the reference's rule) -> int8 codes in
+        // the MMA's operand order, written into the A stage; the unit's
+        // activation scales go into its scale slot.  Work items are (row,
+        // k-block) pairs: a warp takes one row's 256 positions, 8 per lane.
+        const int qw = warp - C::QWARP0;
+        const int Mr = min(p.M, TT);   // one token tile: rows >= Mr never hold data
+        constexpr int TPG = C::GK / 8;                       // lanes per group
+        // Rows >= Mr of every A stage are zero for the whole kernel (the MMA
+        // multiplies them with the weights; the epilogue stores no such row).
+        for (int idx = qw * 32 + lane; idx < C::S_A * C::KS * 2 * (TT - Mr) * 8; idx += C::NQW * 32) {
+            const int c = idx & 7, rr = (idx >> 3) % (TT - Mr), h = ((idx >> 3) / (TT - Mr)) & 1;
+            const int js = ((idx >> 3) / (TT - Mr)) >> 1;    // stage * KS + k-block
+            *reinterpret_cast<uint4*>(a_stage(js / C::KS) + (js % C::KS) * C::A_TILE + h * (TT * 128) +
+                                      (Mr + rr) * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        int xs = 0, stage = 0, slot = 0;
+        uint32_t xph = 0, aph = 0, slph = 0;
+        bool ok = true;
+        Unit un = unit_of(p, u0);
+        for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
+            int kb0, kb1, g0, g1;
+            unit_kblocks<C>(p, un.ut, kb0, kb1);
+            unit_groups<C>(p, un.ut, g0, g1);
+            if (!warp_wait(&bars->sempty[slot], slph ^ 1, abort_flag, p.status, kWQuantSlot)) break;
+            float* asl = slot_as(slot);
+            for (int idx = qw * 32 + lane; idx < (g1 - g0) * (TT - Mr); idx += C::NQW * 32)
+                asl[(idx / (TT - Mr)) * TT + Mr + idx % (TT - Mr)] = 0.0f;
+            for (int kbs = kb0; kbs < kb1; kbs += C::KS) {
+                const int kn = min(C::KS, kb1 - kbs);
+                if (!warp_wait(&bars->xfull[xs], xph, abort_flag, p.status, kWQuantX)) { ok = false; break; }
+                if (!warp_wait(&bars->aempty[stage], aph ^ 1, abort_flag, p.status, kWQuantAEmpty)) { ok = false; break; }
+                const uint8_t* xsm = x_stage(xs);
+                uint8_t* ast = a_stage(stage);
+                for (int it = qw; it < Mr * kn; it += C::NQW) {
+                    const int r = it % Mr, j = it / Mr;
+                    float xv[8];
+                    unpack8_bf16(*reinterpret_cast<const uint4*>(xsm + j * C::X_BOX + r * 512 + lane * 16), xv);
+                    float amax = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(xv[i]));
+#pragma unroll
+                    for (int o = TPG / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                    const uint16_t sb = act_scale_bits(amax);
+                    const float sv = bf16_bits_to_f32(sb);
+                    int q[8];
+                    if (act_scale_fast(sb)) {
+                        const float rcp = __frcp_rn(sv);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) q[i] = quant_fast(xv[i], sv, rcp);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) q[i] = quant_exact(xv[i], sv);
+                    }
+                    // lane l holds positions 8l..8l+7 of the k-block: half l/16, chunk (l%16)/2
+                    *reinterpret_cast<uint2*>(ast + j * C::A_TILE + (lane >> 4) * (TT * 128) + r * 128 +
+                                              ((((lane & 15) >> 1) ^ (r & 7)) << 4) + (lane & 1) * 8) =
+                        pack_operand_order(q);
+                    if ((lane & (TPG - 1)) == 0)
+                        asl[((kbs - kb0 + j) * C::GPK + (lane * 8) / C::GK) * TT + r] = sv;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&bars->afull[stage]);
+                    mbar_arrive(&bars->xempty[xs]);
+                }
+                __syncwarp();
+                if (++xs == C::XS) { xs = 0; xph ^= 1; }
+                if (++stage == C::S_A) { stage = 0; aph ^= 1; }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->sfull[slot]);
+            __syncwarp();
+            if (++slot == C::DS) { slot = 0; slph ^= 1; }
         }
     } else {
         if (C::SPLIT_REGS) regs_inc<C::REGS_EPI>();
@@ -871,11 +987,11 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, 
     }
 }
 
-template <int TT, int GK, bool ASYM, bool PART>
+template <int TT, int GK, bool ASYM, bool PART, bool FQ = false>
 cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pdl, int ws_bf16)
 {
-    using C = Cfg<TT, GK, ASYM>;
-    auto kern = w4a8_gemm_kernel<TT, GK, ASYM, PART>;
+    using C = Cfg<TT, GK, ASYM, FQ>;
+    auto kern = w4a8_gemm_kernel<TT, GK, ASYM, PART, FQ>;
     // The shared-memory opt-in is per device; set it once per device.
     static bool attr_done[64] = {};
     int dev = 0;
@@ -916,6 +1032,14 @@ cudaError_t launch_gk(const GemmParams& p, const GemmConfig& c, int grid, cudaSt
         if constexpr (TT == 16)
             return c.asym ? launch_t<TT, GK, true, true>(p, grid, s, pdl, c.ws_bf16)
                           : launch_t<TT, GK, false, true>(p, grid, s, pdl, c.ws_bf16);
+        else
+            return cudaErrorInvalidValue;
+    }
+    if (c.fq) {
+        // fused quantisation exists for 16-token tiles and GK <= 256 (the host plans it so)
+        if constexpr (TT == 16 && GK <= 256)
+            return c.asym ? launch_t<TT, GK, true, false, true>(p, grid, s, pdl, c.ws_bf16)
+                          : launch_t<TT, GK, false, false, true>(p, grid, s, pdl, c.ws_bf16);
         else
             return cudaErrorInvalidValue;
     }

@@ -71,6 +71,10 @@ struct alignas(64) GemmParams {
     // activations from the quantiser, read with 1-D bulk copies
     const uint8_t* a_tiles;   // [n_tt][kb_total][TT * 256] (gemm_act_tile_offset)
     const float* as_tiles;    // [n_tt][G][TT]
+    // fused quantisation (GemmConfig::fq): the bf16 activation itself, read with
+    // 2-D tensor copies of 256 positions x TT rows (rows >= M and positions >= K
+    // arrive as zeros) and quantised inside the GEMM
+    CUtensorMap tm_x;    // x bf16 [M, K] (row stride ldx), box {256, TT}, no swizzle
     void* out;           // y bf16 [M, N] (row stride ldy), or int32 partials [G, M, N]
     float* partials;     // stream-K partial tiles: [2 * grid][TT][128] fp32
     int* status;         // device status word
@@ -111,6 +115,7 @@ struct GemmConfig {
     bool asym;
     bool ws_bf16;
     bool partials; // debug mode: write int32 group partials instead of y
+    bool fq;       // quantise the activation inside the GEMM (one token tile of 16, GK <= 256)
 };
 
 cudaError_t launch_quant_act(const QuantParams& p, int out_kind, cudaStream_t stream, bool pdl);

@@ -51,44 +51,14 @@ __device__ __forceinline__ int warp_group_sum(int v, int tpg)
     return v;
 }
 
-// quant.py:102-105: bf16(amax / 127), bf16 tiny for an all-zero group.
-__device__ __forceinline__ uint16_t scale_bits_from_amax(float amax)
-{
-    uint16_t sb = f32_to_bf16_bits(__fdiv_rn(amax, 127.0f));
-    if ((sb & 0x7FFFu) == 0) sb = 0x0080u;
-    return sb;
-}
-
-// The layer stack's activation on one element: bf16(silu(g) * u) with
-// silu(g) = g / (1 + exp(-g)) in fp32, as the reference computes it in torch
-// (F.silu(g) * u, npu_ops/python/bench_decode_layer.py:81) before quantising.
-__device__ __forceinline__ float swiglu_bf16(float g, float u)
-{
-    const float a = __fmul_rn(__fdiv_rn(g, 1.0f + expf(-g)), u);
-    return bf16_bits_to_f32(f32_to_bf16_bits(a));
-}
-
 __device__ __forceinline__ void load8_bf16(const uint16_t* xr, int pos, int K, bool vec, float (&v)[8])
 {
     if (vec && pos + 8 <= K) {
-        const uint4 q = *reinterpret_cast<const uint4*>(xr + pos);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            v[2 * i] = __uint_as_float(w[i] << 16);
-            v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-        }
+        unpack8_bf16(*reinterpret_cast<const uint4*>(xr + pos), v);
     } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = pos + i < K ? bf16_bits_to_f32(xr[pos + i]) : 0.0f;
     }
-}
-
-__device__ __forceinline__ int quant_one(float xv, float s)
-{
-    float r = rintf(__fdiv_rn(xv, s));
-    r = fminf(fmaxf(r, -128.0f), 127.0f);
-    return static_cast<int>(r);
 }
 
 template <int kOut>
@@ -149,16 +119,21 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
         for (int w = 0; w < (tpg >> 5); ++w) amax = fmaxf(amax, red_f[w0 + w]);
     }
 
-    const uint16_t sb = scale_bits_from_amax(amax);
+    const uint16_t sb = act_scale_bits(amax);
     const float s = bf16_bits_to_f32(sb);
 
     int q[8];
     int qsum = 0;
+    if (act_scale_fast(sb)) {
+        const float rcp = __frcp_rn(s);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        q[i] = quant_one(xv[i], s);
-        qsum += q[i];
+        for (int i = 0; i < 8; ++i) q[i] = quant_fast(xv[i], s, rcp);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = quant_exact(xv[i], s);
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qsum += q[i];
 
     if (kOut != kOutKernel) {
         qsum = warp_group_sum(qsum, tpg);
@@ -176,11 +151,7 @@ __global__ void __launch_bounds__(kQThreads) quant_act_kernel(const QuantParams 
 
     if (kOut == kOutKernel) {
         // operand order: k0 k2 k4 k6 | k1 k3 k5 k7 (rows >= M and positions >= K are zero)
-        const uint32_t lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) |
-                            (static_cast<uint32_t>(q[6] & 0xFF) << 24);
-        const uint32_t hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) |
-                            (static_cast<uint32_t>(q[7] & 0xFF) << 24);
-        *reinterpret_cast<uint2*>(p.aq + a_off) = make_uint2(lo, hi);
+        *reinterpret_cast<uint2*>(p.aq + a_off) = pack_operand_order(q);
         if (leader && g < p.G) p.as[s_off] = real_row ? s : 0.0f;
     } else if (kOut == kOutPublic) {
         if (!real_row) return;

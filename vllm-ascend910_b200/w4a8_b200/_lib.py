@@ -22,6 +22,7 @@ ERR_TIMEOUT = -6
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
 FIXED_SCRATCH_BYTES = 16 << 20   # W4A8_FIXED_SCRATCH_BYTES
+OPT_NO_FUSED_QUANT = 1           # W4A8_OPT_NO_FUSED_QUANT
 
 _L = None
 
@@ -74,6 +75,7 @@ SIGNATURES = [
     ("w4a8_status_string", ctypes.c_char_p, [ctypes.c_int]),
     ("w4a8_last_cuda_error", ctypes.c_int, []),
     ("w4a8_build_arch", ctypes.c_int, []),
+    ("w4a8_set_options", ctypes.c_int, [_i32]),
 ]
 
 
