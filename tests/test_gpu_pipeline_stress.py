@@ -70,3 +70,36 @@ def test_decode_sweep_graph_replays_without_stall():
     assert not bad, f"replays whose calls recorded a timed-out wait: {bad}"
     for k, v in ys.items():
         assert torch.equal(v, ref[k]), f"call {k} differs from the eager run"
+
+
+# Configurations whose rings put one stage or TMEM buffer in front of both MMA
+# issuers (128-token tiles: 3 activation stages; GK = 1024: several stages per
+# unit).  Before they ran on one issuer, an issuer could match the other's
+# unfinished round by parity and multiply stale activations: 3 of 11 repeated
+# down-projection calls at M = 4096, GK = 256 gave a few wrong token columns in
+# split tiles.  Each case repeats the call and requires identical bits.
+REPEAT_CASES = [  # shape or (N, K), M, gk
+    ("down", 4096, 256), ("down", 2048, 256), ("down", 4096, 128), ("gate_up", 2048, 256),
+    ((1024, 8192), 130, 1024), ((2048, 4096), 48, 1024), ((1024, 8192), 20, 1024), ((2048, 6144), 64, 1024),
+]
+
+
+@pytest.mark.parametrize("case", REPEAT_CASES)
+def test_repeated_calls_identical(case):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from w4a8_b200 import ops
+    from w4a8_b200.synthetic import QWQ_SHAPES, activation_torch, weight_torch
+    shape, M, gk = case
+    K, N = QWQ_SHAPES[shape] if isinstance(shape, str) else (shape[1], shape[0])
+    dev = torch.device("cuda", 0)
+    codes, scale, _ = weight_torch(N, K, gk, 90 + gk, dev)
+    packed = ops.pack_int4_grouped(codes, gk)
+    del codes
+    pw = ops.prepare_weights(packed, scale, None, K, gk)
+    x = activation_torch(M, K, 91 + M, dev)
+    ref = ops.linear_prepared(x, pw)
+    for i in range(12):
+        y = ops.linear_prepared(x, pw) if i % 2 else ops.linear(x, packed, scale, None, gk)
+        assert torch.equal(y, ref), f"call {i + 1} of {case} differs from the first"
+    assert ops.workspace_status(dev) == 0

@@ -118,6 +118,15 @@ struct Cfg {
     static constexpr int S_W_FIT = (kSmemBudget - kBarBytes - DS * SLOT - S_A * A_STAGE - XS * X_STAGE - (FQ ? 1024 : 0)) /
                                    (W_STAGE + WZ_SLOT);
     static constexpr int S_W = S_W_FIT > 16 ? 16 : S_W_FIT;
+    // Two MMA issuers take alternate units only when every activation stage
+    // and every TMEM weight buffer then has one issuer as its only consumer
+    // (one stage per unit, even ring sizes).  An mbarrier wait matches a phase
+    // by parity alone: an issuer that skipped the other issuer's rounds of a
+    // shared stage would take the other's unfinished round r for its own round
+    // r + 1 and multiply stale operands (seen as intermittently wrong token
+    // columns with 128-token tiles, whose ring has 3 stages).  Otherwise one
+    // issuer runs every unit.
+    static constexpr bool TWO_ISSUERS = GK <= 256 && S_A % 2 == 0 && NA % 2 == 0;
     static constexpr int OFF_A = S_W * W_STAGE;
     static constexpr int OFF_WZ = OFF_A + S_A * A_STAGE;
     static constexpr int OFF_SL = OFF_WZ + S_W * WZ_SLOT;
@@ -490,13 +499,14 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
     } else if (warp <= kNumIssuers) {
         if (C::SPLIT_REGS) regs_dec<C::REGS_PRE>();
         // ============================================================ MMA issuers
-        // Issuer i owns the units u0 + i, u0 + i + 2, ...: for those it waits
-        // for the stages, issues every MMA and commits the stages' buffers and
-        // the unit's accumulator slots; for the other issuer's units it only
-        // advances its ring positions.  Each barrier hand-over costs a few
-        // hundred cycles, so splitting whole units halves every issuer's share.
+        // With two issuers (Cfg::TWO_ISSUERS), issuer i owns the units u0 + i,
+        // u0 + i + 2, ...: for those it waits for the stages, issues every MMA
+        // and commits the stages' buffers and the unit's accumulator slots; for
+        // the other issuer's units it only advances its ring positions.  Each
+        // barrier hand-over costs a few hundred cycles, so splitting whole units
+        // halves every issuer's share.  Otherwise issuer 0 owns every unit.
         const int me = warp - 1;
-        if (elect_one()) {
+        if (elect_one() && (C::TWO_ISSUERS || me == 0)) {
             const uint32_t idesc = idesc_i8(128, TT);
             int sa = 0, ab = 0, sl = 0;
             uint32_t saph = 0, abph = 0, slph = 0;
@@ -506,7 +516,7 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
                 int kb0, kb1, g0, g1;
                 unit_kblocks<C>(p, un.ut, kb0, kb1);
                 unit_groups<C>(p, un.ut, g0, g1);
-                const bool mine = ((u - u0) & 1) == me;
+                const bool mine = !C::TWO_ISSUERS || ((u - u0) & 1) == me;
                 for (int kbs = kb0; kbs < kb1; kbs += C::KS) {
                     const int kn = min(C::KS, kb1 - kbs);
                     if (mine) {
