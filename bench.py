@@ -428,15 +428,15 @@ def run_gpu(args, rank, world, local_rank):
     value = world * step_bytes / t_step / 1e9
     t_raw = timed_graph(step_raw, max(3, min(args.steps, 50)), 3)
     raw_value = world * step_bytes / t_raw / 1e9
-    # the same sweep with every call on the standalone quantiser kernel (the
-    # in-GEMM quantisation switched off): what the fused prologue saves
+    # the same sweep with the quantiser fused into the GEMM for the calls with
+    # M <= 16 (W4A8_OPT_FUSED_QUANT; off by default because it measures slower)
     from w4a8_b200 import _lib
-    old_opt = _lib.lib().w4a8_set_options(_lib.OPT_NO_FUSED_QUANT)
+    old_opt = _lib.lib().w4a8_set_options(_lib.OPT_FUSED_QUANT)
     try:
-        t_sq = timed_graph(step, max(3, min(args.steps, 50)), 3)
+        t_fq = timed_graph(step, max(3, min(args.steps, 50)), 3)
     finally:
         _lib.lib().w4a8_set_options(old_opt)
-    sq_value = world * step_bytes / t_sq / 1e9
+    fq_value = world * step_bytes / t_fq / 1e9
     status = ops.workspace_status(dev)
 
     # ---- end to end through the public op, host buffers ----
@@ -518,10 +518,10 @@ def run_gpu(args, rank, world, local_rank):
         "e2e": e2e,
         "raw_layout": {"value": raw_value, "unit": "GB/s", "ms_per_step": 1e3 * t_raw,
                        "note": "same sweep on the reference row-major weight layout (2-D tensor copies)"},
-        "standalone_quant": {"value": sq_value, "unit": "GB/s", "ms_per_step": 1e3 * t_sq,
-                             "note": "same sweep with the activation quantised by its own kernel before every "
-                                     "GEMM (W4A8_OPT_NO_FUSED_QUANT); by default calls with M <= 16 quantise "
-                                     "inside the GEMM"},
+        "fused_quant": {"value": fq_value, "unit": "GB/s", "ms_per_step": 1e3 * t_fq,
+                        "note": "same sweep with the 16 calls of M <= 16 quantising their activation inside the "
+                                "GEMM (W4A8_OPT_FUSED_QUANT) instead of in the standalone quantiser kernel that "
+                                "the headline uses"},
         "gpu_launches": launches,
         "clocks": clocks,
         "prefill": {"metric": "W4A8 GEMM int8 TOP/s (prefill)", "value": pre_tops, "unit": "TOP/s",
@@ -540,10 +540,9 @@ def run_gpu(args, rank, world, local_rank):
 
 
 def kernels_per_call(M, N, K, sms, gk=GK):
-    """Kernels one linear call launches: the quantiser (unless the call
-    quantises inside the GEMM: M <= 16, GK <= 256, aligned rows), the GEMM and,
-    when the GEMM's stream-K split leaves a tile divided between CTAs, the
-    fix-up kernel (the host plan in csrc/w4a8_capi.cu)."""
+    """Kernels one linear call launches: the quantiser, the GEMM and, when the
+    GEMM's stream-K split leaves a tile divided between CTAs, the fix-up kernel
+    (the host plan in csrc/w4a8_capi.cu)."""
     tt = 16 if M <= 16 else (32 if M <= 32 else (64 if M <= 64 else 128))
     G = -(-K // gk)
     last = K - (G - 1) * gk
@@ -553,8 +552,7 @@ def kernels_per_call(M, N, K, sms, gk=GK):
     units = -(-N // 128) * -(-M // tt) * upt
     grid = max(1, min(sms, units))
     split = any((c * units // grid) % upt for c in range(1, grid))
-    fused = tt == 16 and gk <= 256 and M <= 16 and K % 8 == 0      # quantiser inside the GEMM
-    return (1 if fused else 2) + (1 if split else 0)
+    return 2 + (1 if split else 0)
 
 
 def profile_sweep():

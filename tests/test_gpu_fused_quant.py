@@ -1,8 +1,8 @@
-"""The activation quantiser fused into the GEMM (calls with M <= 16, group
-size <= 256, 16-byte aligned rows) against the standalone quantiser kernel
-followed by the GEMM (w4a8_set_options(W4A8_OPT_NO_FUSED_QUANT)): the same
-codes, scales and accumulation order, so the same bits; and both against the
-oracle at the linear tolerance."""
+"""The activation quantiser fused into the GEMM (w4a8_set_options(
+W4A8_OPT_FUSED_QUANT); calls with M <= 16, group size <= 256, 16-byte aligned
+rows) against the default path, the standalone quantiser kernel followed by
+the GEMM: the same codes, scales and accumulation order, so the same bits; and
+both against the oracle at the linear tolerance."""
 import numpy as np
 import pytest
 
@@ -40,14 +40,14 @@ def test_fused_equals_standalone(orc, M, N, K, gk, asym, prepared):
         return ops.linear_prepared(x, pw) if prepared else ops.linear(x, packed, scale, wz, gk)
 
     L = _lib.lib()
-    fused = run()
-    old = L.w4a8_set_options(_lib.OPT_NO_FUSED_QUANT)
+    standalone = run()
+    old = L.w4a8_set_options(_lib.OPT_FUSED_QUANT)
     try:
-        standalone = run()
+        fused = run()
+        assert torch.equal(run(), fused)             # repeatable
     finally:
         L.w4a8_set_options(old)
     assert torch.equal(fused, standalone)
-    assert torch.equal(run(), fused)                 # repeatable
     assert ops.workspace_status() == 0
     # the oracle on a column sample
     cols = np.unique(np.concatenate([np.arange(0, N, 128), np.arange(127, N, 128)]))
@@ -64,6 +64,15 @@ def test_fused_in_graph_and_strided_rows(orc):
     path; replaying a captured graph with new activation values recomputes."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
+    from w4a8_b200 import _lib
+    old = _lib.lib().w4a8_set_options(_lib.OPT_FUSED_QUANT)
+    try:
+        _fused_graph_case()
+    finally:
+        _lib.lib().w4a8_set_options(old)
+
+
+def _fused_graph_case():
     from w4a8_b200 import ops
     from w4a8_b200 import synthetic as syn
     dev = torch.device("cuda", 0)

@@ -313,12 +313,13 @@ bool cached_x_map(const void* x, int64_t M, int64_t K, int64_t ldx, CUtensorMap*
 // Library options (w4a8_set_options).
 int g_options = 0;
 
-// Whether a linear call quantises its activation inside the GEMM: one 16-token
-// tile (M <= 16), GK <= 256, and an activation the 2-D tensor copies can read
-// (16-byte aligned rows).  Everything else runs the standalone quantiser first.
+// Whether a linear call quantises its activation inside the GEMM: only with
+// W4A8_OPT_FUSED_QUANT set, and then for one 16-token tile (M <= 16), GK <= 256
+// and an activation the 2-D tensor copies can read (16-byte aligned rows).
+// Everything else runs the standalone quantiser first.
 bool fused_quant_ok(const Plan& pl, const void* x, int64_t ldx, bool swiglu)
 {
-    return !(g_options & W4A8_OPT_NO_FUSED_QUANT) && !swiglu && pl.tt == 16 && pl.n_tt == 1 && pl.gk <= 256 &&
+    return (g_options & W4A8_OPT_FUSED_QUANT) && !swiglu && pl.tt == 16 && pl.n_tt == 1 && pl.gk <= 256 &&
            aligned(x, 16) && ldx % 8 == 0;
 }
 

@@ -22,7 +22,7 @@ ERR_TIMEOUT = -6
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
 FIXED_SCRATCH_BYTES = 16 << 20   # W4A8_FIXED_SCRATCH_BYTES
-OPT_NO_FUSED_QUANT = 1           # W4A8_OPT_NO_FUSED_QUANT
+OPT_FUSED_QUANT = 1              # W4A8_OPT_FUSED_QUANT
 
 _L = None
 
