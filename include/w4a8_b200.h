@@ -221,6 +221,29 @@ W4A8_API int w4a8_ar_allreduce_bf16(w4a8_ar* h, const void* in, void* out, int64
 W4A8_API int w4a8_ar_status(w4a8_ar* h, int32_t reset);
 W4A8_API int w4a8_ar_destroy(w4a8_ar* h);
 
+/* ---- row-parallel linear fused with its all-reduce (tensor parallelism) ----
+ * y = sum over the ranks of ar's group, in rank order in fp32 and rounded once
+ * to bf16, of this rank's w4a8_linear_prepared result (x: the rank's K shard;
+ * act = W4A8_ACT_SWIGLU takes x = [gate | up] as w4a8_linear_prepared_swiglu).
+ * Every rank calls it in the same order with the same M and N, like
+ * w4a8_ar_allreduce_bf16; M * N * 2 <= w4a8_ar_max_bytes(ar), (M * N) % 8 == 0,
+ * y dense [M, N] and 16-byte aligned.  The GEMM's epilogue (and its stream-K
+ * fix-up, for output tiles split between CTAs) stores each finished bf16 tile
+ * straight into every rank's receive slot with plain peer stores, and one
+ * reduction kernel then publishes this rank's flags, waits (bounded, 1 s) for
+ * the others' and sums: the local round trip of the partial output and the
+ * all-reduce's copy pass are gone.  The same bits as w4a8_linear_prepared
+ * followed by w4a8_ar_allreduce_bf16.  A wait that runs out leaves y
+ * untouched and is reported by w4a8_ar_status.  Replaces the reference's
+ * row-parallel GEMM + peer all-reduce pair, fused as its design notes
+ * propose (MGCKPT/P6.5_TP.md:900-957; npu_ops/kernel/peer_allreduce_f32.cpp:127-270). */
+#define W4A8_ACT_NONE 0
+#define W4A8_ACT_SWIGLU 1
+W4A8_API int w4a8_linear_prepared_allreduce(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N,
+                                            int32_t group_size, const void* prepared, int32_t w_scale_dtype,
+                                            int32_t has_zero, int32_t act, void* y, void* workspace,
+                                            size_t workspace_bytes, w4a8_ar* ar, void* stream);
+
 /* ---- status ---- */
 /* Synchronises `stream` and returns the device status word of `workspace`
  * (0 = no kernel reported a failure; otherwise 0x100 + the id of the wait

@@ -7,7 +7,8 @@ fallback.  MODE ``skew``: the reference's barrier gates -- ranks desynchronised
 on purpose (skewed launches, changing values, a 200-call run, graph replays,
 24 live graphs) -- plus a strided and a misaligned message, which take the
 staged form of the one-shot path on one rank while the other passes a dense
-tensor.  MODE ``absent``: rank 1 stays alive but skips the last call; rank 0's
+tensor.  MODE ``fused``: the row-parallel linear fused with the all-reduce
+against the linear followed by the all-reduce, bit for bit.  MODE ``absent``: rank 1 stays alive but skips the last call; rank 0's
 wait must run out and ``check()`` must raise (no GPU fault, no hang).
 """
 import datetime
@@ -184,6 +185,63 @@ def skew_gates(ar, rank, world, dev, verdict):
     verdict["calls_custom"], verdict["calls_fallback"] = ar.calls_custom, ar.calls_fallback
 
 
+def fused_gates(ar, rank, world, dev, verdict):
+    """Row-parallel shards of one seeded layer (each rank holds K/world columns):
+    the fused linear + all-reduce against the linear followed by the one-shot
+    all-reduce, bit for bit, for plain and SwiGLU inputs, several M (one beyond
+    the message limit, NCCL), and replays of a captured graph with new inputs."""
+    from w4a8_b200 import ops, tp
+    from w4a8_b200 import synthetic as syn
+    gk = 128
+    cases = [(5120, 5120, None), (5120, 27648, "swiglu")]      # (N, full K, act): o_proj, down
+    ok = True
+    for N, Kf, act in cases:
+        g = torch.Generator(device=dev).manual_seed(1234 + N + Kf)
+        codes = torch.randint(-8, 8, (N, Kf), generator=g, device=dev, dtype=torch.int16).to(torch.int8)
+        scale = torch.exp(torch.randn(Kf // gk, N, generator=g, device=dev) * 0.5 - 6.0)
+        c, sc = tp.row_shard(codes, scale, rank, world, gk)
+        K = Kf // world
+        pw = ops.prepare_weights(ops.pack_int4_grouped(c.contiguous(), gk), sc.contiguous(), None, K, gk)
+        for M in (1, 16, 64, 200):
+            x = syn.activation_torch(M, 2 * K if act else K, 50 + M + 7 * rank, dev)
+            y = ar.linear_prepared(x, pw, act=act)
+            ref = ops.linear_prepared(x, pw, act=act)
+            ar(ref)
+            torch.cuda.synchronize()
+            if not torch.equal(y, ref):
+                ok = False
+                verdict["msgs"].append(["fused != linear + all-reduce", N, Kf, M, act])
+        # graph: capture once, replay with new inputs
+        M = 16
+        x = syn.activation_torch(M, 2 * K if act else K, 90 + rank, dev)
+        ar.linear_prepared(x, pw, act=act)
+        torch.cuda.synchronize()
+        dist.barrier()
+        gr = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gr, stream=s):
+                yg = ar.linear_prepared(x, pw, act=act)
+        torch.cuda.current_stream().wait_stream(s)
+        for rep in range(5):
+            x.copy_(syn.activation_torch(M, 2 * K if act else K, 100 + rep + 7 * rank, dev))
+            torch.cuda.synchronize()
+            dist.barrier()
+            gr.replay()
+            torch.cuda.synchronize()
+            ref = ops.linear_prepared(x, pw, act=act)
+            ar(ref)
+            torch.cuda.synchronize()
+            if not torch.equal(yg, ref):
+                ok = False
+                verdict["msgs"].append(["graph replay differs", N, rep])
+        del gr
+        ar.check()
+    verdict["ok"] &= ok
+    verdict["calls_fused"] = ar.calls_fused
+
+
 def main():
     rank, world, port, mode, out = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3], sys.argv[4], sys.argv[5]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=port)
@@ -286,6 +344,8 @@ def main():
             ar.check()
         elif mode == "skew":
             skew_gates(ar, rank, world, dev, verdict)
+        elif mode == "fused":
+            fused_gates(ar, rank, world, dev, verdict)
         elif mode == "absent":
             t = inputs(rank, 5120, 0).to(dev)
             ar(t)

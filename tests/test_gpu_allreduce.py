@@ -59,6 +59,44 @@ def test_absent_peer_times_out_and_leaves_output():
         h1.destroy()
 
 
+@pytest.mark.parametrize("M,N,K,act", [(16, 5120, 2560, None), (5, 640, 3456, "swiglu"), (64, 5120, 640, None),
+                                        (1, 1024, 1024, "swiglu")])
+def test_world1_fused_row_linear_equals_linear(M, N, K, act):
+    """One rank: the fused row-parallel linear + all-reduce gives the linear's bits
+    (the sum of one slot), on two calls in a row (the bank alternates)."""
+    from w4a8_b200 import _lib, ops
+    from w4a8_b200 import synthetic as syn
+    from w4a8_b200.allreduce import _Handle
+    dev = _dev()
+    gk = 128
+    codes, scale, _ = syn.weight_torch(N, K, gk, 7 + K, dev)
+    pw = ops.prepare_weights(ops.pack_int4_grouped(codes, gk), scale, None, K, gk)
+    h = _Handle(0, 1, 1 << 20)
+    try:
+        h.open_local([h])
+        L = _lib.lib()
+        for call in range(2):
+            x = syn.activation_torch(M, 2 * K if act else K, 8 + call, dev)
+            ref = ops.linear_prepared(x, pw, act=act)
+            y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)
+            ws, wsb = ops.workspace(ops._ws_bytes(M, N, K, gk), dev)
+            rc = L.w4a8_linear_prepared_allreduce(
+                x.data_ptr(), M, K, x.stride(0), N, gk, pw.ptr(), pw.ws_dtype, 0,
+                _lib.ACT_SWIGLU if act else _lib.ACT_NONE, y.data_ptr(), ws, wsb, h.h,
+                torch.cuda.current_stream().cuda_stream)
+            assert rc == 0, L.w4a8_status_string(rc).decode()
+            torch.cuda.synchronize()
+            assert torch.equal(y, ref), call
+            assert h.status() == 0 and ops.workspace_status() == 0
+        with pytest.raises(RuntimeError):                 # M * N * 2 beyond the buffer
+            _lib.check(L.w4a8_linear_prepared_allreduce(
+                x.data_ptr(), 1024, K, x.stride(0), N, gk, pw.ptr(), pw.ws_dtype, 0, 0, y.data_ptr(), ws, wsb,
+                h.h, None), "oversize")
+    finally:
+        torch.cuda.synchronize()
+        h.destroy()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -106,6 +144,22 @@ def test_all_gpus_skewed_barrier_gates(tmp_path):
     if world < 3:
         pytest.skip("needs three or more GPUs")
     for v in _run("skew", tmp_path, world, timeout=420):
+        assert v["ok"], v
+
+
+def test_two_gpus_fused_row_linear(tmp_path):
+    """Row-parallel linear fused with the all-reduce on 2 ranks: the same bits as
+    the linear followed by the one-shot all-reduce; eager and graph replays."""
+    for v in _run("fused", tmp_path, 2):
+        assert v["ok"], v
+        assert v["calls_fused"] >= 8, v
+
+
+def test_all_gpus_fused_row_linear(tmp_path):
+    world = min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 0
+    if world < 3:
+        pytest.skip("needs three or more GPUs")
+    for v in _run("fused", tmp_path, world):
         assert v["ok"], v
 
 

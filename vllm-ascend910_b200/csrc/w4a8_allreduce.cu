@@ -38,6 +38,7 @@
 #include <new>
 
 #include "w4a8_b200.h"
+#include "w4a8_kernels.h"
 
 namespace {
 
@@ -178,6 +179,77 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_bf16(const Params 
     }
 }
 
+// The reduction half of the fused row-parallel linear: the GEMM (and its
+// stream-K fix-up) already stored this rank's message into slot [bank][rank]
+// of every rank (PushParams), so the push pass of the one-shot kernel is gone.
+// Per block b: wait for the pushing kernels to finish (programmatic dependent
+// launch), make their peer stores visible system-wide, publish seq into
+// flag[rank][b] of every rank, wait (bounded) for every source's flag, then sum
+// slice b of the bank in rank order.  The same bank, flag and counter protocol
+// as allreduce_oneshot_bf16, so pushed and ordinary calls can interleave.
+template <int W>
+__global__ void __launch_bounds__(kThreads) allreduce_pushed_bf16(const Params p)
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int b = blockIdx.x;
+    uint8_t* mine = p.base[p.rank];
+    uint32_t* counter = reinterpret_cast<uint32_t*>(mine + p.off_counter) + b;
+    __shared__ uint32_t s_seq;
+    __shared__ int s_abort;
+    if (threadIdx.x == 0) {
+        s_seq = *counter + 1u;
+        s_abort = 0;
+    }
+    __syncthreads();
+    const uint32_t seq = s_seq;
+    const size_t bank_off = (seq & 1u) * p.bank_bytes;
+    const int64_t e0 = static_cast<int64_t>(b) * p.per_block < p.count ? static_cast<int64_t>(b) * p.per_block : p.count;
+    const int64_t e1 = e0 + p.per_block < p.count ? e0 + p.per_block : p.count;
+    const int64_t v0 = e0 / 8, v1 = e1 / 8;
+    if (threadIdx.x < W) {
+        // the previous grids' peer stores are ordered before this release
+        __threadfence_system();
+        uint32_t* f = reinterpret_cast<uint32_t*>(p.base[threadIdx.x] + p.off_flags) + p.rank * kMaxBlocks + b;
+        store_release_sys(f, seq);
+        const uint32_t* g = reinterpret_cast<const uint32_t*>(mine + p.off_flags) + threadIdx.x * kMaxBlocks + b;
+        const uint64_t t0 = now_ns();
+        while (static_cast<int32_t>(load_acquire_sys(g) - seq) < 0) {
+            if (now_ns() - t0 > kWaitNs) {
+                atomicCAS(reinterpret_cast<int*>(mine + p.off_status), 0, 1);
+                s_abort = 1;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *counter = seq;
+    if (s_abort) return;
+    const uint8_t* bank = mine + bank_off;
+    for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {
+        uint4 v[W];
+#pragma unroll
+        for (int r = 0; r < W; ++r) v[r] = reinterpret_cast<const uint4*>(bank + static_cast<size_t>(r) * p.slot_bytes)[i];
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+        for (int r = 0; r < W; ++r) {
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[r]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(h[j]);
+                acc[2 * j] += f.x;
+                acc[2 * j + 1] += f.y;
+            }
+        }
+        uint4 o;
+        __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+        reinterpret_cast<uint4*>(p.out)[i] = o;
+    }
+}
+
 }  // namespace
 
 struct w4a8_ar {
@@ -189,6 +261,74 @@ struct w4a8_ar {
     bool ipc[kMaxRanks] = {};               // mapped[r] came from cudaIpcOpenMemHandle
     bool opened = false;
 };
+
+namespace {
+
+Params make_params(const w4a8_ar* h, const void* in, void* out, int64_t count)
+{
+    Params p{};
+    for (int r = 0; r < h->world; ++r) p.base[r] = h->mapped[r];
+    p.in = static_cast<const __nv_bfloat16*>(in);
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.count = count;
+    // Always kMaxBlocks blocks (trailing slices may be empty): every block
+    // then advances its call counter on every call, so all blocks of a call
+    // share one sequence number and the slot parity alternates uniformly
+    // whatever the message sizes of successive calls.
+    p.per_block = ((count + kMaxBlocks - 1) / kMaxBlocks + 7) / 8 * 8;
+    p.slot_bytes = h->lay.slot_bytes;
+    p.bank_bytes = h->lay.bank_bytes;
+    p.off_flags = h->lay.off_flags;
+    p.off_counter = h->lay.off_counter;
+    p.off_status = h->lay.off_status;
+    p.rank = h->rank;
+    p.world = h->world;
+    return p;
+}
+
+}  // namespace
+
+namespace w4a8 {
+
+int ar_push_params(const w4a8_ar* h, size_t bytes, PushParams* out)
+{
+    if (!h || !out || bytes > h->max_bytes || (h->world > 1 && !h->opened)) return W4A8_ERR_INVALID;
+    PushParams q{};
+    for (int r = 0; r < h->world; ++r) q.base[r] = h->mapped[r];
+    q.counter = reinterpret_cast<const uint32_t*>(h->local + h->lay.off_counter);
+    q.slot_bytes = h->lay.slot_bytes;
+    q.bank_bytes = h->lay.bank_bytes;
+    q.world = h->world;
+    q.rank = h->rank;
+    *out = q;
+    return W4A8_OK;
+}
+
+cudaError_t ar_launch_reduce_pushed(w4a8_ar* h, void* out, int64_t count, cudaStream_t st)
+{
+    const Params p = make_params(h, nullptr, out, count);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kMaxBlocks);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    switch (h->world) {
+        case 1: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<1>, p);
+        case 2: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<2>, p);
+        case 3: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<3>, p);
+        case 4: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<4>, p);
+        case 5: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<5>, p);
+        case 6: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<6>, p);
+        case 7: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<7>, p);
+        default: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<8>, p);
+    }
+}
+
+}  // namespace w4a8
 
 extern "C" {
 
@@ -272,23 +412,7 @@ int w4a8_ar_allreduce_bf16(w4a8_ar* h, const void* in, void* out, int64_t count,
     if (count % 8 || static_cast<size_t>(count) * 2 > h->max_bytes) return W4A8_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) return W4A8_ERR_INVALID;
     if (h->world > 1 && !h->opened) return W4A8_ERR_INVALID;
-    Params p{};
-    for (int r = 0; r < h->world; ++r) p.base[r] = h->mapped[r];
-    p.in = static_cast<const __nv_bfloat16*>(in);
-    p.out = static_cast<__nv_bfloat16*>(out);
-    p.count = count;
-    // Always kMaxBlocks blocks (trailing slices may be empty): every block
-    // then advances its call counter on every call, so all blocks of a call
-    // share one sequence number and the slot parity alternates uniformly
-    // whatever the message sizes of successive calls.
-    p.per_block = ((count + kMaxBlocks - 1) / kMaxBlocks + 7) / 8 * 8;
-    p.slot_bytes = h->lay.slot_bytes;
-    p.bank_bytes = h->lay.bank_bytes;
-    p.off_flags = h->lay.off_flags;
-    p.off_counter = h->lay.off_counter;
-    p.off_status = h->lay.off_status;
-    p.rank = h->rank;
-    p.world = h->world;
+    const Params p = make_params(h, in, out, count);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (h->world) {
         case 1: allreduce_oneshot_bf16<1><<<kMaxBlocks, kThreads, 0, st>>>(p); break;

@@ -324,10 +324,11 @@ bool fused_quant_ok(const Plan& pl, const void* x, int64_t ldx, bool swiglu)
 }
 
 int run_gemm(const Plan& pl, const Weights& w, void* out, int64_t ldy, bool partials, uint8_t* ws, cudaStream_t st,
-             const void* fq_x = nullptr, int64_t fq_ldx = 0)
+             const void* fq_x = nullptr, int64_t fq_ldx = 0, const PushParams* push = nullptr)
 {
     GemmParams g;
     std::memset(&g, 0, sizeof(g));
+    if (push) g.push = *push;
     if (fq_x) {
         if (get_encoder() != W4A8_OK) return fail_cuda(cudaErrorNotSupported);
         if (!cached_x_map(fq_x, pl.M, pl.K, fq_ldx, &g.tm_x)) return W4A8_ERR_INVALID;
@@ -778,6 +779,36 @@ int w4a8_linear_prepared_swiglu(const void* gu, int64_t M, int64_t K, int64_t ld
 {
     return linear_prepared_impl(gu, M, K, ldx, N, gk, prepared, ws_dtype, has_zero, y, ldy, workspace,
                                 workspace_bytes, stream, true);
+}
+
+int w4a8_linear_prepared_allreduce(const void* x, int64_t M, int64_t K, int64_t ldx, int64_t N, int32_t gk,
+                                   const void* prepared, int32_t ws_dtype, int32_t has_zero, int32_t act, void* y,
+                                   void* workspace, size_t workspace_bytes, w4a8_ar* ar, void* stream)
+{
+    int rc = check_common(M, N, K, gk);
+    if (rc != W4A8_OK) return rc;
+    if (act != W4A8_ACT_NONE && act != W4A8_ACT_SWIGLU) return W4A8_ERR_UNSUPPORTED;
+    if (!ar) return W4A8_ERR_INVALID;
+    const bool swiglu = act == W4A8_ACT_SWIGLU;
+    if (M == 0) return W4A8_OK;
+    if (!x || ldx < (swiglu ? 2 * K : K) || !aligned(x, 2)) return W4A8_ERR_INVALID;
+    if (!prepared || !aligned(prepared, 256)) return W4A8_ERR_INVALID;
+    if (ws_dtype != W4A8_DTYPE_BF16 && ws_dtype != W4A8_DTYPE_F32) return W4A8_ERR_UNSUPPORTED;
+    // y is the reduced [M, N] message: dense, 16-byte aligned, whole 8-element vectors
+    if (!y || !aligned(y, 16) || (M * N) % 8 != 0) return W4A8_ERR_INVALID;
+    PushParams pp;
+    if ((rc = ar_push_params(ar, static_cast<size_t>(M) * N * 2, &pp)) != W4A8_OK) return rc;
+    int sms = 0;
+    if ((rc = device_info(&sms)) != W4A8_OK) return rc;
+    const Plan pl = make_plan(M, N, K, gk, sms);
+    if (!workspace || !aligned(workspace, 1024) || workspace_bytes < pl.total) return W4A8_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st, swiglu)) != W4A8_OK) return rc;
+    const Weights w{nullptr, nullptr, nullptr, static_cast<const uint8_t*>(prepared), has_zero != 0, ws_dtype};
+    if ((rc = run_gemm(pl, w, nullptr, N, false, ws, st, nullptr, 0, &pp)) != W4A8_OK) return rc;
+    const cudaError_t e = ar_launch_reduce_pushed(ar, y, M * N, st);
+    return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
 }
 
 int w4a8_linear_gemm_prepared(int64_t M, int64_t K, int64_t N, int32_t gk, const void* prepared, int32_t ws_dtype,

@@ -283,6 +283,31 @@ __device__ __noinline__ void store_partials(const GemmParams& p, R16 r, int g, i
     }
 }
 
+// The fused all-reduce's output path: element (m, n) of this rank's bf16 result
+// goes to slot [bank][rank] of every rank's all-reduce buffer (a dense [M, N]
+// message; plain stores, over NVLink for the peers).  The bank is the parity of
+// the all-reduce call this result belongs to: the counter of completed calls
+// plus one, read after the kernel's dependency wait (this thread reaches here
+// only after that wait, through the pipeline's barriers).
+__device__ __forceinline__ __nv_bfloat16* push_slot(const PushParams& pp, int r)
+{
+    const uint32_t seq = *reinterpret_cast<const volatile uint32_t*>(pp.counter) + 1u;
+    return reinterpret_cast<__nv_bfloat16*>(pp.base[r] + (seq & 1u) * pp.bank_bytes +
+                                            static_cast<size_t>(pp.rank) * pp.slot_bytes);
+}
+
+template <int NC>
+__device__ __forceinline__ void push_tile(const GemmParams& p, int m0, int n, const uint64_t (&acc2)[NC / 2])
+{
+    if (n >= p.N) return;
+    for (int r = 0; r < p.push.world; ++r) {
+        __nv_bfloat16* dst = push_slot(p.push, r);
+#pragma unroll
+        for (int j = 0; j < NC; ++j)
+            if (m0 + j < p.M) dst[static_cast<int64_t>(m0 + j) * p.N + n] = __float2bfloat16_rn(acc_at(acc2, j));
+    }
+}
+
 // End of a CTA's share of one output tile: store the bf16 tile when the CTA
 // computed all of it, else store its fp32 part for w4a8_splitk_reduce_kernel
 // (which runs after the GEMM, so no fence or arrival count is needed here).
@@ -295,6 +320,10 @@ __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, 
     const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
     const int n = un.wt * 128 + row;
     if (u0 <= tfirst && u1 - 1 >= tlast) {
+        if (p.push.world) {
+            push_tile<NC>(p, un.tt * TT + col0, n, acc2);
+            return;
+        }
         __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
         for (int j = 0; j < NC; ++j) {
@@ -988,6 +1017,18 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, 
             for (int q = 0; q < 4; ++q)
 #pragma unroll
                 for (int j = 0; j < 16; ++j) sum[j] += v[q][j];
+        }
+        if (p.push.world) {
+            if (n < p.N)
+                for (int r = 0; r < p.push.world; ++r) {
+                    __nv_bfloat16* dst = push_slot(p.push, r);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int m = tt * TT + c0 + j;
+                        if (m < p.M) dst[static_cast<int64_t>(m) * p.N + n] = __float2bfloat16_rn(sum[j]);
+                    }
+                }
+            return;
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {

@@ -58,6 +58,16 @@ __host__ __device__ inline int64_t gemm_act_tile_offset(int row, int pos, int tt
            ((c ^ (r & 7)) << 4) + b;
 }
 
+// Row-parallel output pushed to every rank (the fused GEMM + all-reduce): the
+// bf16 result tile goes straight into slot [bank][rank] of every rank's
+// one-shot all-reduce buffer instead of into y.  world == 0: no push.
+struct PushParams {
+    uint8_t* base[8];          // every rank's buffer as mapped in this process (own included)
+    const uint32_t* counter;   // this rank's call counter of the all-reduce (block 0's)
+    size_t slot_bytes, bank_bytes;
+    int world, rank;
+};
+
 // The GEMM's view of one call.  Tensor maps are built on the host.
 struct alignas(64) GemmParams {
     // raw (reference-layout) weights, read with 2-D tensor copies
@@ -78,6 +88,7 @@ struct alignas(64) GemmParams {
     void* out;           // y bf16 [M, N] (row stride ldy), or int32 partials [G, M, N]
     float* partials;     // stream-K partial tiles: [2 * grid][TT][128] fp32
     int* status;         // device status word
+    PushParams push;     // (fused all-reduce) where finished bf16 tiles go instead of out
     int M, N, Kpad, G;
     int64_t ldy;
     int n_wt, n_tt, units_per_tile, total_units, kb_total;
@@ -131,5 +142,14 @@ size_t gemm_smem_bytes(const GemmConfig& cfg);
 // Sums the parts of output tiles split across GEMM CTAs (a programmatic
 // dependent of the GEMM launched with the same parameters and grid).
 cudaError_t launch_splitk_reduce(const GemmParams& p, int tt, int grid, cudaStream_t stream);
+
+// The one-shot all-reduce's side of the fused row-parallel linear
+// (w4a8_allreduce.cu): where a GEMM must push a message of `bytes`, and the
+// reduction that follows the pushes (flags, bounded waits, rank-order sum).
+}  // namespace w4a8
+struct w4a8_ar;
+namespace w4a8 {
+int ar_push_params(const w4a8_ar* h, size_t bytes, PushParams* out);
+cudaError_t ar_launch_reduce_pushed(w4a8_ar* h, void* out, int64_t count, cudaStream_t stream);
 
 }  // namespace w4a8

@@ -23,6 +23,8 @@ DTYPE_BF16 = 0
 DTYPE_F32 = 1
 FIXED_SCRATCH_BYTES = 16 << 20   # W4A8_FIXED_SCRATCH_BYTES
 OPT_FUSED_QUANT = 1              # W4A8_OPT_FUSED_QUANT
+ACT_NONE = 0                     # W4A8_ACT_NONE
+ACT_SWIGLU = 1                   # W4A8_ACT_SWIGLU
 
 _L = None
 
@@ -71,6 +73,8 @@ SIGNATURES = [
     ("w4a8_ar_allreduce_bf16", ctypes.c_int, [_p, _p, _p, _i64, _p]),
     ("w4a8_ar_status", ctypes.c_int, [_p, _i32]),
     ("w4a8_ar_destroy", ctypes.c_int, [_p]),
+    ("w4a8_linear_prepared_allreduce", ctypes.c_int,
+     [_p, _i64, _i64, _i64, _i64, _i32, _p, _i32, _i32, _i32, _p, _p, _sz, _p, _p]),
     ("w4a8_workspace_status", ctypes.c_int, [_p, _i32, _p]),
     ("w4a8_status_string", ctypes.c_char_p, [ctypes.c_int]),
     ("w4a8_last_cuda_error", ctypes.c_int, []),

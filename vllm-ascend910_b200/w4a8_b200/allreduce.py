@@ -104,6 +104,7 @@ class CustomAllReduce:
         self.calls_custom = 0
         self.calls_staged = 0
         self.calls_fallback = 0
+        self.calls_fused = 0
 
     def fits(self, t: torch.Tensor) -> bool:
         return eligible(t.numel(), t.dtype, self.max_bytes)
@@ -125,6 +126,36 @@ class CustomAllReduce:
             import torch.distributed as dist
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
             self.calls_fallback += 1
+
+    def linear_prepared(self, x: torch.Tensor, pw, act: Optional[str] = None) -> torch.Tensor:
+        """A row-parallel linear and its all-reduce: the sum over the ranks of
+        ``ops.linear_prepared(x, pw, act=act)``, every rank calling with its own
+        K shard (``w4a8_linear_prepared_allreduce``: the GEMM stores its output
+        tiles straight into every rank's receive slot, one kernel then sums).
+        Messages larger than ``max_bytes`` take the linear followed by NCCL.
+        The same bits as the linear followed by ``self(y)``."""
+        from . import ops
+        K = pw.K
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) != 1:
+            x2 = x2.contiguous()
+        M, N = x2.shape[0], pw.N
+        if self.world == 1 or not eligible(M * N, torch.bfloat16, self.max_bytes) or M == 0:
+            y = ops.linear_prepared(x2, pw, act=act)
+            self(y)
+            return y.reshape(*x.shape[:-1], N)
+        want = 2 * K if act == "swiglu" else K
+        if x2.dtype != torch.bfloat16 or x2.shape[1] != want:
+            raise RuntimeError(f"row-parallel linear: x must be bf16 [M, {want}]")
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=x2.device)
+        ws, wsb = ops.workspace(ops._ws_bytes(M, N, K, pw.group_size), x2.device)
+        rc = _lib.lib().w4a8_linear_prepared_allreduce(
+            x2.data_ptr(), M, K, x2.stride(0), N, pw.group_size, pw.ptr(), pw.ws_dtype, 1 if pw.has_zero else 0,
+            _lib.ACT_SWIGLU if act == "swiglu" else _lib.ACT_NONE, y.data_ptr(), ws, wsb, self._h.h,
+            torch.cuda.current_stream(x2.device).cuda_stream)
+        _lib.check(rc, "w4a8_linear_prepared_allreduce")
+        self.calls_fused += 1
+        return y.reshape(*x.shape[:-1], N)
 
     def check(self) -> None:
         """Raise if a kernel wait for a peer ran out (synchronises the device)."""

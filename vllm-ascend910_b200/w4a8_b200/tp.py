@@ -189,24 +189,42 @@ def cuda_swiglu_linear(gu: torch.Tensor, w: ShardWeights) -> torch.Tensor:
     return ops.linear(gu, w.packed, w.scale, None, GK, act="swiglu")
 
 
+# (x, w, act) -> the all-reduced output of a row-parallel linear; act None or "swiglu"
+RowLinear = Callable[[torch.Tensor, ShardWeights, Optional[str]], torch.Tensor]
+
+
+def composed_row_linear(linear: Linear, swiglu_linear: SwigluLinear, allreduce: AllReduce) -> RowLinear:
+    """The row-parallel linear, then the all-reduce as its own step."""
+    def f(x, w, act=None):
+        y = swiglu_linear(x, w) if act == "swiglu" else linear(x, w)
+        allreduce(y)
+        return y
+    return f
+
+
+def fused_row_linear(car) -> RowLinear:
+    """The row-parallel linear fused with the one-shot all-reduce
+    (``CustomAllReduce.linear_prepared``) on prepared weights."""
+    return lambda x, w, act=None: car.linear_prepared(x, w.prepared, act=act)
+
+
 def layer_forward(h: torch.Tensor, L: LayerShard, tp: int, linear: Linear, allreduce: AllReduce,
-                  d: Dims = QWQ, swiglu_linear: Optional[SwigluLinear] = None) -> torch.Tensor:
+                  d: Dims = QWQ, swiglu_linear: Optional[SwigluLinear] = None,
+                  row_linear: Optional[RowLinear] = None) -> torch.Tensor:
     swiglu_linear = swiglu_linear or composed_swiglu_linear(linear)
+    row_linear = row_linear or composed_row_linear(linear, swiglu_linear, allreduce)
     qkv = linear(h, L.qkv)
     att = qkv[:, : d.hidden // tp]                     # attention stand-in: the rank's q section
-    o = linear(att, L.o)
-    allreduce(o)
+    o = row_linear(att, L.o, None)
     gu = linear(o, L.gate_up)
-    dn = swiglu_linear(gu, L.down)
-    allreduce(dn)
-    return dn
+    return row_linear(gu, L.down, "swiglu")
 
 
 def stack_forward(h: torch.Tensor, layers: Sequence[LayerShard], tp: int, linear: Linear,
-                  allreduce: AllReduce, d: Dims = QWQ,
-                  swiglu_linear: Optional[SwigluLinear] = None) -> torch.Tensor:
+                  allreduce: AllReduce, d: Dims = QWQ, swiglu_linear: Optional[SwigluLinear] = None,
+                  row_linear: Optional[RowLinear] = None) -> torch.Tensor:
     for L in layers:
-        h = layer_forward(h, L, tp, linear, allreduce, d, swiglu_linear)
+        h = layer_forward(h, L, tp, linear, allreduce, d, swiglu_linear, row_linear)
     return h
 
 
@@ -272,8 +290,9 @@ def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4,
     The step is captured in a CUDA graph (the all-reduces included); the time is
     the max over ranks of CUDA-event time per forward.  Returns tokens/s (M per
     forward) and layer-tokens/s (M x layers per forward) with the roofline
-    fraction, per all-reduce (``nccl``, or ``custom``: the one-shot kernel for
-    small messages, NCCL for the rest).
+    fraction, per all-reduce (``nccl``; ``custom``: the one-shot kernel for
+    small messages, NCCL for the rest; ``fused``: the row-parallel linears fused
+    with the one-shot all-reduce, ``custom`` beyond its message limit).
 
     With ``parity`` and world > 1, rank 0 also runs the unsharded stack (tp = 1,
     the same seeded weights and inputs) and reports, per all-reduce and M, how
@@ -286,18 +305,22 @@ def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4,
                    "applies silu(gate)*up in its activation quantiser"}
     outs = {}
     for mode in allreduces if world > 1 else ("none",):
-        car = None
+        car, row = None, None
         if world == 1:
             ar = (lambda t: None)
-        elif mode == "custom":
+        elif mode in ("custom", "fused"):
             car = custom_allreduce()
             ar = car
+            if mode == "fused":
+                row = fused_row_linear(car)
         else:
             ar = nccl_allreduce()
         key = "per_M" if mode in ("nccl", "none") else f"per_M_{mode}"
-        out[key], outs[mode] = _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops)
+        out[key], outs[mode] = _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops, row)
         if car is not None:
             car.check()
+            if mode == "fused":
+                out["fused_calls"] = car.calls_fused
             car.close()
     del Ls
     if parity and world > 1:
@@ -340,7 +363,7 @@ def _stack_input(M: int, d: Dims, dev) -> torch.Tensor:
     return torch.randn(M, d.hidden, generator=gen, device=dev).to(torch.bfloat16)
 
 
-def _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops):
+def _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops, row=None):
     import torch.distributed as dist
     layers = len(Ls)
     res, outs = [], {}
@@ -348,7 +371,7 @@ def _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops):
         h0 = _stack_input(M, d, dev)
 
         def fwd():
-            return stack_forward(h0, Ls, world, cuda_linear, ar, d, cuda_swiglu_linear)
+            return stack_forward(h0, Ls, world, cuda_linear, ar, d, cuda_swiglu_linear, row)
 
         for _ in range(2):
             fwd()
