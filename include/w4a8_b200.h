@@ -229,10 +229,11 @@ W4A8_API int w4a8_ar_destroy(w4a8_ar* h);
  * w4a8_ar_allreduce_bf16; M * N * 2 <= w4a8_ar_max_bytes(ar), (M * N) % 8 == 0,
  * y dense [M, N] and 16-byte aligned.  The GEMM's epilogue (and its stream-K
  * fix-up, for output tiles split between CTAs) stores each finished bf16 tile
- * straight into every rank's receive slot with plain peer stores, and one
+ * straight into this rank's receive slot of the all-reduce buffer, and one
  * reduction kernel then publishes this rank's flags, waits (bounded, 1 s) for
- * the others' and sums: the local round trip of the partial output and the
- * all-reduce's copy pass are gone.  The same bits as w4a8_linear_prepared
+ * the others' and sums every rank's slot in place with peer loads: the
+ * partial output's own buffer and the all-reduce's copy pass are gone
+ * (W4A8_OPT_AR_PUSH: the epilogue stores into every rank's slot instead).  The same bits as w4a8_linear_prepared
  * followed by w4a8_ar_allreduce_bf16.  A wait that runs out leaves y
  * untouched and is reported by w4a8_ar_status.  Replaces the reference's
  * row-parallel GEMM + peer all-reduce pair, fused as its design notes
@@ -262,8 +263,12 @@ W4A8_API int w4a8_build_arch(void);
  * bits.  Off by default: every CTA quantises the activation slice of each
  * weight tile it visits, and measured on B200 the fused call is slower at
  * every decode size (e.g. gate_up M = 16: 183 us against 34 us per call).
+ * W4A8_OPT_AR_PUSH: w4a8_linear_prepared_allreduce stores every output tile
+ * into every rank's receive slot (posted peer stores from the GEMM epilogue)
+ * instead of its own slot only, the peers then reading it (the default).
  * Returns the previous flags. */
 #define W4A8_OPT_FUSED_QUANT 1
+#define W4A8_OPT_AR_PUSH 2
 W4A8_API int w4a8_set_options(int32_t flags);
 
 #ifdef __cplusplus

@@ -189,7 +189,20 @@ def fused_gates(ar, rank, world, dev, verdict):
     """Row-parallel shards of one seeded layer (each rank holds K/world columns):
     the fused linear + all-reduce against the linear followed by the one-shot
     all-reduce, bit for bit, for plain and SwiGLU inputs, several M (one beyond
-    the message limit, NCCL), and replays of a captured graph with new inputs."""
+    the message limit, NCCL), and replays of a captured graph with new inputs;
+    with the epilogue storing into its own slot (peers read it, the default)
+    and into every rank's slot (W4A8_OPT_AR_PUSH)."""
+    from w4a8_b200 import _lib
+    for opt in (0, _lib.OPT_AR_PUSH):
+        old = _lib.lib().w4a8_set_options(opt)
+        try:
+            _fused_cases(ar, rank, world, dev, verdict, "push" if opt else "pull")
+        finally:
+            _lib.lib().w4a8_set_options(old)
+    verdict["calls_fused"] = ar.calls_fused
+
+
+def _fused_cases(ar, rank, world, dev, verdict, variant):
     from w4a8_b200 import ops, tp
     from w4a8_b200 import synthetic as syn
     gk = 128
@@ -210,7 +223,7 @@ def fused_gates(ar, rank, world, dev, verdict):
             torch.cuda.synchronize()
             if not torch.equal(y, ref):
                 ok = False
-                verdict["msgs"].append(["fused != linear + all-reduce", N, Kf, M, act])
+                verdict["msgs"].append(["fused != linear + all-reduce", variant, N, Kf, M, act])
         # graph: capture once, replay with new inputs
         M = 16
         x = syn.activation_torch(M, 2 * K if act else K, 90 + rank, dev)
@@ -235,11 +248,10 @@ def fused_gates(ar, rank, world, dev, verdict):
             torch.cuda.synchronize()
             if not torch.equal(yg, ref):
                 ok = False
-                verdict["msgs"].append(["graph replay differs", N, rep])
+                verdict["msgs"].append(["graph replay differs", variant, N, rep])
         del gr
         ar.check()
     verdict["ok"] &= ok
-    verdict["calls_fused"] = ar.calls_fused
 
 
 def main():

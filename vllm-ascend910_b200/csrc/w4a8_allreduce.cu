@@ -187,7 +187,9 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_bf16(const Params 
 // flag[rank][b] of every rank, wait (bounded) for every source's flag, then sum
 // slice b of the bank in rank order.  The same bank, flag and counter protocol
 // as allreduce_oneshot_bf16, so pushed and ordinary calls can interleave.
-template <int W>
+// PULL: every rank's GEMM wrote only its own slot (locally), so the sum reads
+// slot [bank][r] from rank r's buffer (peer loads) instead of from this rank's.
+template <int W, bool PULL>
 __global__ void __launch_bounds__(kThreads) allreduce_pushed_bf16(const Params p)
 {
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -224,11 +226,13 @@ __global__ void __launch_bounds__(kThreads) allreduce_pushed_bf16(const Params p
     __syncthreads();
     if (threadIdx.x == 0) *counter = seq;
     if (s_abort) return;
-    const uint8_t* bank = mine + bank_off;
     for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {
         uint4 v[W];
 #pragma unroll
-        for (int r = 0; r < W; ++r) v[r] = reinterpret_cast<const uint4*>(bank + static_cast<size_t>(r) * p.slot_bytes)[i];
+        for (int r = 0; r < W; ++r) {
+            const uint8_t* src = (PULL ? p.base[r] : mine) + bank_off + static_cast<size_t>(r) * p.slot_bytes;
+            v[r] = PULL ? __ldcv(reinterpret_cast<const uint4*>(src) + i) : reinterpret_cast<const uint4*>(src)[i];
+        }
         float acc[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.f;
@@ -290,21 +294,22 @@ Params make_params(const w4a8_ar* h, const void* in, void* out, int64_t count)
 
 namespace w4a8 {
 
-int ar_push_params(const w4a8_ar* h, size_t bytes, PushParams* out)
+int ar_push_params(const w4a8_ar* h, size_t bytes, bool pull, PushParams* out)
 {
     if (!h || !out || bytes > h->max_bytes || (h->world > 1 && !h->opened)) return W4A8_ERR_INVALID;
     PushParams q{};
-    for (int r = 0; r < h->world; ++r) q.base[r] = h->mapped[r];
+    // pull: the GEMM writes only this rank's own slot (one destination, local)
+    q.world = pull ? 1 : h->world;
+    for (int r = 0; r < q.world; ++r) q.base[r] = pull ? h->local : h->mapped[r];
     q.counter = reinterpret_cast<const uint32_t*>(h->local + h->lay.off_counter);
     q.slot_bytes = h->lay.slot_bytes;
     q.bank_bytes = h->lay.bank_bytes;
-    q.world = h->world;
     q.rank = h->rank;
     *out = q;
     return W4A8_OK;
 }
 
-cudaError_t ar_launch_reduce_pushed(w4a8_ar* h, void* out, int64_t count, cudaStream_t st)
+cudaError_t ar_launch_reduce_pushed(w4a8_ar* h, void* out, int64_t count, bool pull, cudaStream_t st)
 {
     const Params p = make_params(h, nullptr, out, count);
     cudaLaunchConfig_t cfg = {};
@@ -316,15 +321,27 @@ cudaError_t ar_launch_reduce_pushed(w4a8_ar* h, void* out, int64_t count, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (pull) {
+        switch (h->world) {
+            case 1: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<1, true>, p);
+            case 2: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<2, true>, p);
+            case 3: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<3, true>, p);
+            case 4: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<4, true>, p);
+            case 5: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<5, true>, p);
+            case 6: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<6, true>, p);
+            case 7: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<7, true>, p);
+            default: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<8, true>, p);
+        }
+    }
     switch (h->world) {
-        case 1: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<1>, p);
-        case 2: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<2>, p);
-        case 3: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<3>, p);
-        case 4: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<4>, p);
-        case 5: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<5>, p);
-        case 6: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<6>, p);
-        case 7: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<7>, p);
-        default: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<8>, p);
+        case 1: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<1, false>, p);
+        case 2: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<2, false>, p);
+        case 3: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<3, false>, p);
+        case 4: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<4, false>, p);
+        case 5: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<5, false>, p);
+        case 6: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<6, false>, p);
+        case 7: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<7, false>, p);
+        default: return cudaLaunchKernelEx(&cfg, allreduce_pushed_bf16<8, false>, p);
     }
 }
 

@@ -797,7 +797,8 @@ int w4a8_linear_prepared_allreduce(const void* x, int64_t M, int64_t K, int64_t 
     // y is the reduced [M, N] message: dense, 16-byte aligned, whole 8-element vectors
     if (!y || !aligned(y, 16) || (M * N) % 8 != 0) return W4A8_ERR_INVALID;
     PushParams pp;
-    if ((rc = ar_push_params(ar, static_cast<size_t>(M) * N * 2, &pp)) != W4A8_OK) return rc;
+    const bool pull = !(g_options & W4A8_OPT_AR_PUSH);
+    if ((rc = ar_push_params(ar, static_cast<size_t>(M) * N * 2, pull, &pp)) != W4A8_OK) return rc;
     int sms = 0;
     if ((rc = device_info(&sms)) != W4A8_OK) return rc;
     const Plan pl = make_plan(M, N, K, gk, sms);
@@ -807,7 +808,7 @@ int w4a8_linear_prepared_allreduce(const void* x, int64_t M, int64_t K, int64_t 
     if ((rc = run_quant_kernel_layout(pl, x, ldx, ws, st, swiglu)) != W4A8_OK) return rc;
     const Weights w{nullptr, nullptr, nullptr, static_cast<const uint8_t*>(prepared), has_zero != 0, ws_dtype};
     if ((rc = run_gemm(pl, w, nullptr, N, false, ws, st, nullptr, 0, &pp)) != W4A8_OK) return rc;
-    const cudaError_t e = ar_launch_reduce_pushed(ar, y, M * N, st);
+    const cudaError_t e = ar_launch_reduce_pushed(ar, y, M * N, pull, st);
     return e == cudaSuccess ? W4A8_OK : fail_cuda(e);
 }
 

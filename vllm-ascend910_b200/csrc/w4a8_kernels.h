@@ -149,7 +149,9 @@ cudaError_t launch_splitk_reduce(const GemmParams& p, int tt, int grid, cudaStre
 }  // namespace w4a8
 struct w4a8_ar;
 namespace w4a8 {
-int ar_push_params(const w4a8_ar* h, size_t bytes, PushParams* out);
-cudaError_t ar_launch_reduce_pushed(w4a8_ar* h, void* out, int64_t count, cudaStream_t stream);
+// pull: the GEMM stores into this rank's own slot only and the reduction reads
+// the peers' slots; otherwise the GEMM stores into every rank's slot.
+int ar_push_params(const w4a8_ar* h, size_t bytes, bool pull, PushParams* out);
+cudaError_t ar_launch_reduce_pushed(w4a8_ar* h, void* out, int64_t count, bool pull, cudaStream_t stream);
 
 }  // namespace w4a8

@@ -23,6 +23,7 @@ DTYPE_BF16 = 0
 DTYPE_F32 = 1
 FIXED_SCRATCH_BYTES = 16 << 20   # W4A8_FIXED_SCRATCH_BYTES
 OPT_FUSED_QUANT = 1              # W4A8_OPT_FUSED_QUANT
+OPT_AR_PUSH = 2                  # W4A8_OPT_AR_PUSH
 ACT_NONE = 0                     # W4A8_ACT_NONE
 ACT_SWIGLU = 1                   # W4A8_ACT_SWIGLU
 
