@@ -483,7 +483,7 @@ def run_gpu(args, rank, world, local_rank):
     if not args.no_tp_stack:
         from w4a8_b200 import tp as tpmod
         tp = tpmod.bench_stack(world, rank, dev, ms=(16, 256, 4096), layers=4, iters=max(3, min(args.steps, 20)),
-                               hbm_gbs=hbm_peak, i8_tops=i8_peak, allreduces=("nccl", "custom", "fused"))
+                               hbm_gbs=hbm_peak, i8_tops=i8_peak, allreduces=("nccl", "custom", "fused", "fused_push"))
 
     if rank != 0:
         return

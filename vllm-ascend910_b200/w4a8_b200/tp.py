@@ -314,21 +314,28 @@ def bench_stack(world: int, rank: int, dev, ms=(16, 256, 4096), layers: int = 4,
                                    cuda_swiglu_linear).float()
         del L1
     per = []
+    from . import _lib
     for mode in allreduces if world > 1 else ("none",):
         car, row = None, None
         if world == 1:
             ar = (lambda t: None)
-        elif mode in ("custom", "fused"):
+        elif mode in ("custom", "fused", "fused_push"):
             car = custom_allreduce()
             ar = car
-            if mode == "fused":
+            if mode != "custom":
                 row = fused_row_linear(car)
         else:
             ar = nccl_allreduce()
-        key = "per_M" if mode in ("nccl", "none") else f"per_M_{mode}"
-        out[key], outs = _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops, row)
-        if parity and world > 1:
-            per += _stack_parity(world, rank, dev, Ls[:1], ms, d, ar, row, mode, outs, ref)
+        # fused_push: the epilogue stores into every rank's slot (W4A8_OPT_AR_PUSH)
+        old_opt = _lib.lib().w4a8_set_options(_lib.OPT_AR_PUSH) if mode == "fused_push" else None
+        try:
+            key = "per_M" if mode in ("nccl", "none") else f"per_M_{mode}"
+            out[key], outs = _time_stack(world, dev, Ls, ms, iters, ar, d, hbm_gbs, i8_tops, row)
+            if parity and world > 1:
+                per += _stack_parity(world, rank, dev, Ls[:1], ms, d, ar, row, mode, outs, ref)
+        finally:
+            if old_opt is not None:
+                _lib.lib().w4a8_set_options(old_opt)
         if car is not None:
             car.check()
             if mode == "fused":
