@@ -209,8 +209,12 @@ __global__ void __launch_bounds__(kThreads) allreduce_pushed_bf16(const Params p
     const int64_t e1 = e0 + p.per_block < p.count ? e0 + p.per_block : p.count;
     const int64_t v0 = e0 / 8, v1 = e1 / 8;
     if (threadIdx.x < W) {
-        // the previous grids' peer stores are ordered before this release
-        __threadfence_system();
+        // Push: the previous grids stored into peers' memory over NVLink; a
+        // system-scope fence orders those stores before this release.  Pull:
+        // the stores were local and had reached this GPU's L2 when the grid
+        // completed, and peers read them there after acquiring the flag, so the
+        // fence (several microseconds per call, measured) is not needed.
+        if (!PULL) __threadfence_system();
         uint32_t* f = reinterpret_cast<uint32_t*>(p.base[threadIdx.x] + p.off_flags) + p.rank * kMaxBlocks + b;
         store_release_sys(f, seq);
         const uint32_t* g = reinterpret_cast<const uint32_t*>(mine + p.off_flags) + threadIdx.x * kMaxBlocks + b;
