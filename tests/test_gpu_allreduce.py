@@ -60,7 +60,7 @@ def test_absent_peer_times_out_and_leaves_output():
 
 
 @pytest.mark.parametrize("M,N,K,act", [(16, 5120, 2560, None), (5, 640, 3456, "swiglu"), (64, 5120, 640, None),
-                                        (1, 1024, 1024, "swiglu")])
+                                        (1, 1024, 1024, "swiglu"), (100, 5120, 1280, None)])
 def test_world1_fused_row_linear_equals_linear(M, N, K, act):
     """One rank: the fused row-parallel linear + all-reduce gives the linear's bits
     (the sum of one slot), on two calls in a row (the bank alternates)."""

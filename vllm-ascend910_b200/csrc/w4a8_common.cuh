@@ -252,6 +252,27 @@ __device__ __forceinline__ void reg_fence16(uint32_t (&r)[16])
                  "+r"(r[14]), "+r"(r[15]));
 }
 
+// 32 lanes x 8 / x 4 consecutive 32-bit columns (narrow token tiles).
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t* r)
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
+__device__ __forceinline__ void tc_ld4(uint32_t taddr, uint32_t* r)
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+}
+
+// reg_fence16 for 4 registers.
+__device__ __forceinline__ void reg_fence4(uint32_t* r)
+{
+    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]));
+}
+
 __device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8])
 {
     asm volatile(

@@ -53,7 +53,7 @@ enum { kWProdEmpty = 1, kWActEmpty, kWProdSlot, kWConvFull, kWConvAEmpty, kWMmaF
 // and four more warps quantise each stage straight into the MMA operand
 // buffer and the unit's scale slot.  Built for one 16-token tile (decode),
 // GK <= 256.
-template <int TT_, int GK_, bool ASYM_, bool FQ_ = false>
+template <int TT_, int GK_, bool ASYM_, bool FQ_ = false, int E_ = 0>
 struct Cfg {
     static constexpr int TT = TT_;
     static constexpr int GK = GK_;
@@ -68,9 +68,9 @@ struct Cfg {
     static constexpr int UKB = GK <= 256 ? KS : GK / 256;    // k-blocks per unit (max)
     static constexpr int GPU = GK <= 256 ? KS * GPK : 1;     // groups per unit (max)
     static constexpr bool SYM16 = !ASYM && GK <= 256;
-    static constexpr int E = TT <= 16 ? 1 : 2;               // epilogue warpgroups
+    static constexpr int E = E_ ? E_ : (TT <= 16 ? 1 : 2);   // epilogue warpgroups
     static constexpr int NC = TT / E;                        // accumulator columns per thread
-    static constexpr int NCH = NC / 16;                      // 16-column TMEM chunks per thread
+    static constexpr int NCH = NC >= 16 ? NC / 16 : 1;       // 16-column TMEM chunks per thread
     static constexpr int NQW = FQ ? 4 : 0;                   // quantiser warps
     static constexpr int QWARP0 = kNumPreWarps + 4 * E;      // first quantiser warp
     static constexpr int THREADS = (kNumPreWarps + 4 * E + NQW) * 32;
@@ -127,6 +127,13 @@ struct Cfg {
     // columns with 128-token tiles, whose ring has 3 stages).  Otherwise one
     // issuer runs every unit.
     static constexpr bool TWO_ISSUERS = GK <= 256 && S_A % 2 == 0 && NA % 2 == 0;
+    // With two issuers the accumulator slots are split between them too
+    // (issuer i owns the slots i, i + 2, ...), so neither ever waits on a slot
+    // phase of the other's: an issuer that only watched the other's slots
+    // could fall two phases behind one of them once the epilogue outpaces the
+    // MMA, and then wait for a phase that never comes.
+    static constexpr int NRING = TWO_ISSUERS ? NACC / 2 : NACC;   // slots per issuer
+    __host__ __device__ static constexpr int acc_slot(int i, int who) { return TWO_ISSUERS ? 2 * i + who : i; }
     static constexpr int OFF_A = S_W * W_STAGE;
     static constexpr int OFF_WZ = OFF_A + S_A * A_STAGE;
     static constexpr int OFF_SL = OFF_WZ + S_W * WZ_SLOT;
@@ -136,8 +143,9 @@ struct Cfg {
     static constexpr int TMEM_COLS = 512;
     static_assert(S_W >= 3 && S_A >= 2, "pipeline too shallow");
     static_assert(NACC >= 2, "need at least two accumulator slots");
+    static_assert(!TWO_ISSUERS || (NACC % 2 == 0 && NRING >= 2), "two slots per issuer");
     static_assert(GPU % CG == 0, "slots split a unit evenly");
-    static_assert(NC % 16 == 0, "epilogue works in 16-column chunks");
+    static_assert(NC % 16 == 0 || NC == 8, "epilogue works in 16-column chunks (or 8 columns per thread)");
     static_assert(TOTCH % BCH == 0, "slots split into whole batches");
     static_assert(OFF_A % 1024 == 0 && OFF_WZ % 1024 == 0, "tile alignment");
     static_assert(SMEM <= 227 * 1024, "shared memory");
@@ -264,6 +272,25 @@ __device__ __forceinline__ void rescale_chunk(uint64_t (&acc2)[NC / 2], int i, c
     }
 }
 
+// rescale_chunk for the first NV columns (NV a multiple of 4) of one group.
+template <int NC, int NV>
+__device__ __forceinline__ void rescale_cols(uint64_t (&acc2)[NC / 2], const uint32_t* r, float wsv, const float* asg)
+{
+    const uint64_t ws2 = pack2(wsv, wsv);
+#pragma unroll
+    for (int j = 0; j < NV; j += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(asg + j);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint64_t f2 = pack2(__int2float_rn(static_cast<int>(r[j + 2 * h])),
+                                      __int2float_rn(static_cast<int>(r[j + 2 * h + 1])));
+            const uint64_t c2 = f2_mul(ws2, h == 0 ? pack2(a4.x, a4.y) : pack2(a4.z, a4.w));
+            uint64_t& a = acc2[j / 2 + h];
+            a = f2_fma(f2, c2, a);
+        }
+    }
+}
+
 __device__ __forceinline__ float acc_at(const uint64_t* acc2, int j)
 {
     return __uint_as_float(static_cast<uint32_t>(acc2[j >> 1] >> ((j & 1) * 32)));
@@ -296,14 +323,14 @@ __device__ __forceinline__ __nv_bfloat16* push_slot(const PushParams& pp, int r)
                                             static_cast<size_t>(pp.rank) * pp.slot_bytes);
 }
 
-template <int NC>
+template <int NC, int NV>
 __device__ __forceinline__ void push_tile(const GemmParams& p, int m0, int n, const uint64_t (&acc2)[NC / 2])
 {
     if (n >= p.N) return;
     for (int r = 0; r < p.push.world; ++r) {
         __nv_bfloat16* dst = push_slot(p.push, r);
 #pragma unroll
-        for (int j = 0; j < NC; ++j)
+        for (int j = 0; j < NV; ++j)
             if (m0 + j < p.M) dst[static_cast<int64_t>(m0 + j) * p.N + n] = __float2bfloat16_rn(acc_at(acc2, j));
     }
 }
@@ -311,7 +338,10 @@ __device__ __forceinline__ void push_tile(const GemmParams& p, int m0, int n, co
 // End of a CTA's share of one output tile: store the bf16 tile when the CTA
 // computed all of it, else store its fp32 part for w4a8_splitk_reduce_kernel
 // (which runs after the GEMM, so no fence or arrival count is needed here).
-template <class C>
+// Only the first NV columns hold results (the rest are past M).  PUSH: the
+// fused all-reduce's instantiation, whose finished tiles go to the ranks'
+// receive slots instead of y.
+template <class C, int NV, bool PUSH>
 __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, int u0, int u1, int cta, int row,
                                            int col0, const uint64_t (&acc2)[C::NC / 2])
 {
@@ -320,13 +350,13 @@ __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, 
     const int tfirst = t * p.units_per_tile, tlast = tfirst + p.units_per_tile - 1;
     const int n = un.wt * 128 + row;
     if (u0 <= tfirst && u1 - 1 >= tlast) {
-        if (p.push.world) {
-            push_tile<NC>(p, un.tt * TT + col0, n, acc2);
+        if constexpr (PUSH) {
+            push_tile<NC, NV>(p, un.tt * TT + col0, n, acc2);
             return;
         }
         __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
-        for (int j = 0; j < NC; ++j) {
+        for (int j = 0; j < NV; ++j) {
             const int m = un.tt * TT + col0 + j;
             if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(acc_at(acc2, j));
         }
@@ -335,17 +365,184 @@ __device__ __forceinline__ void flush_tile(const GemmParams& p, const Unit& un, 
     const int side = (t == u0 / p.units_per_tile) ? 0 : 1;
     float* mine = p.partials + static_cast<int64_t>(2 * cta + side) * (TT * 128);
 #pragma unroll
-    for (int j = 0; j < NC; ++j) __stcg(mine + (col0 + j) * 128 + row, acc_at(acc2, j));
+    for (int j = 0; j < NV; ++j) __stcg(mine + (col0 + j) * 128 + row, acc_at(acc2, j));
+}
+
+// The epilogue warps' loop.  NV: token columns rescaled per thread -- all NC,
+// or (16-token tiles of calls with at most 4 or 8 tokens) only the first NV:
+// the MMA still multiplies 16 token columns (its smallest N at 128 rows), but
+// the columns past M hold zeros and are neither rescaled nor stored.
+template <class C, bool PART, int NV, bool PUSH>
+__device__ __forceinline__ void epilogue_role(const GemmParams& p, Bars* bars, uint8_t* smem, uint32_t tbase,
+                                              volatile int* abort_flag, int ws_bf16, int warp, int lane, int u0,
+                                              int u1, int cta)
+{
+    constexpr int TT = C::TT;
+    constexpr bool NARROW = NV < 16;     // one batch of x4 / x8 loads per slot
+    static_assert(NV <= C::NC && (!NARROW || (C::TT == 16 && !PART && (NV == 4 || NV == 8))),
+                  "narrow columns: 16-token tiles");
+    auto slot_ws = [&](int s) { return smem + C::OFF_SL + s * C::SLOT; };
+    auto slot_as = [&](int s) { return reinterpret_cast<float*>(slot_ws(s) + C::r128(C::SL_WS)); };
+    const int ew = warp - kNumPreWarps;
+    const int quarter = warp & 3;
+    const int part = ew >> 2;
+    const int row = quarter * 32 + lane;
+    const int col0 = part * NV;                   // NV == NC unless the tile has fewer tokens
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    constexpr int NCH = C::NCH;
+
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0)
+        for (int b = 0; b < C::NACC; ++b) mbar_arrive(&bars->accempty[b]);
+    __syncwarp();
+
+    uint64_t acc2[C::NC / 2];
+#pragma unroll
+    for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
+    // Accumulator slot ring position of the unit's issuer (sl, aph) and of the
+    // other issuer (sl_o, aph_o): with two issuers units alternate between them
+    // and each fills its own slots (Cfg::acc_slot), so the pair swaps per unit.
+    int sl = 0, sl_o = 0, slot = 0;
+    uint32_t aph = 0, aph_o = 0, slph = 0;
+    bool ok = true;
+    Unit un = unit_of(p, u0);
+    for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
+        int g0, g1;
+        unit_groups<C>(p, un.ut, g0, g1);
+        const int who = C::TWO_ISSUERS ? (u - u0) & 1 : 0;
+        if (!warp_wait(&bars->sfull[slot], slph, abort_flag, p.status, kWEpiSlot)) { ok = false; break; }
+        const uint8_t* wsb = slot_ws(slot);
+        const float* asb = slot_as(slot);
+        // one accumulator slot holds CG groups: all of this unit's, or one
+        for (int gs = g0; gs < g1; gs += C::CG) {
+            const int ps = C::acc_slot(sl, who);
+            if (!warp_wait(&bars->accfull[ps], aph, abort_flag, p.status, kWEpiAccFull)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t t_slot = tbase + lane_off + C::ACC0 + static_cast<uint32_t>(ps * C::CG * TT + col0);
+            // this row's weight scale of each group in the slot, read once
+            float wsv[C::CG];
+            if (!PART) {
+#pragma unroll
+                for (int gi = 0; gi < C::CG; ++gi) {
+                    const int gl = min(gs + gi, g1 - 1) - g0;
+                    wsv[gi] = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gl * 128 + row])
+                                      : reinterpret_cast<const float*>(wsb)[gl * 128 + row];
+                    if (C::SYM16) wsv[gi] *= 0.0625f;   // the unpack carried weights as 16*w
+                }
+            }
+            if constexpr (NARROW) {
+                // every group of the slot in one batch of loads; the slot goes
+                // back to the MMA as soon as the values are in registers
+                uint32_t r[C::CG][NV];
+#pragma unroll
+                for (int gi = 0; gi < C::CG; ++gi) {
+                    if constexpr (NV == 8)
+                        tc_ld8(t_slot + gi * TT, r[gi]);
+                    else
+                        tc_ld4(t_slot + gi * TT, r[gi]);
+                }
+                tc_wait_ld();
+#pragma unroll
+                for (int gi = 0; gi < C::CG; ++gi)
+#pragma unroll
+                    for (int q = 0; q < NV; q += 4) reg_fence4(r[gi] + q);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->accempty[ps]);
+                __syncwarp();
+#pragma unroll
+                for (int gi = 0; gi < C::CG; ++gi)
+                    if (gs + gi < g1) rescale_cols<C::NC, NV>(acc2, r[gi], wsv[gi], asb + (gs + gi - g0) * TT + col0);
+            } else {
+                // Batches of BCH chunks, software-pipelined: the next batch's
+                // tcgen05.ld is in flight while this batch is rescaled.  With
+                // EARLY_RELEASE the slot goes back to the MMA as soon as its last
+                // batch is in registers, otherwise after the rescale.
+                R16 r[2][C::BCH];
+    #pragma unroll
+                for (int q = 0; q < C::BCH; ++q)
+                    tc_ld16(t_slot + (q / NCH) * TT + 16 * (q % NCH), r[0][q].v);
+                tc_wait_ld();
+    #pragma unroll
+                for (int q = 0; q < C::BCH; ++q) reg_fence16(r[0][q].v);
+    #pragma unroll
+                for (int b = 0; b < C::NB; ++b) {
+                    if (b + 1 < C::NB) {
+    #pragma unroll
+                        for (int q = 0; q < C::BCH; ++q) {
+                            const int c = (b + 1) * C::BCH + q;
+                            tc_ld16(t_slot + (c / NCH) * TT + 16 * (c % NCH), r[(b + 1) & 1][q].v);
+                        }
+                    } else if (C::EARLY_RELEASE) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bars->accempty[ps]);
+                        __syncwarp();
+                    }
+    #pragma unroll
+                    for (int q = 0; q < C::BCH; ++q) {
+                        const int c = b * C::BCH + q, gi = c / NCH, i = c % NCH;
+                        const int g = gs + gi;
+                        if (g >= g1) continue;
+                        const int gl = g - g0;           // group index within the unit's scale entry
+                        if (PART)
+                            store_partials<C::SYM16>(p, r[b & 1][q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
+                        else
+                            rescale_chunk<C::NC>(acc2, i, r[b & 1][q], wsv[gi], asb + gl * TT + col0 + 16 * i);
+                    }
+                    if (b + 1 < C::NB) {
+                        tc_wait_ld();
+    #pragma unroll
+                        for (int q = 0; q < C::BCH; ++q) reg_fence16(r[(b + 1) & 1][q].v);
+                    }
+                }
+                if (!C::EARLY_RELEASE) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->accempty[ps]);
+                    __syncwarp();
+                }
+            }
+            if (++sl == C::NRING) { sl = 0; aph ^= 1; }
+        }
+        if (!ok) break;
+        if (C::TWO_ISSUERS) {
+            const int ts = sl;
+            sl = sl_o;
+            sl_o = ts;
+            const uint32_t tp = aph;
+            aph = aph_o;
+            aph_o = tp;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->sempty[slot]);
+        __syncwarp();
+        if (++slot == C::DS) { slot = 0; slph ^= 1; }
+
+        // ---- end of this CTA's share of tile t: store or hand over ----
+        if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
+            if (!PART) flush_tile<C, NV, PUSH>(p, un, u0, u1, cta, row, col0, acc2);
+#pragma unroll
+            for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
+        }
+    }
 }
 
 // PART: the debug mode that writes each group's exact int32 partials instead
 // of y.  It is a separate instantiation (16-token tiles only) so the product
 // epilogue carries no call and no second output path.
-template <int TT, int GK, bool ASYM, bool PART, bool FQ>
-__global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
+//
+// NV: token columns the epilogue rescales (0: all of the tile).  A call of at
+// most 4 or 8 tokens runs a 16-token instantiation with NV = 4 or 8; the
+// variants are separate kernels so the common case carries no extra code.
+template <int TT, int GK, bool ASYM, bool PART, bool FQ, int NV, int EPI, bool PUSH>
+__global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ, EPI>::THREADS, 1)
     w4a8_gemm_kernel(const __grid_constant__ GemmParams p, const int ws_bf16)
 {
-    using C = Cfg<TT, GK, ASYM, FQ>;
+    using C = Cfg<TT, GK, ASYM, FQ, EPI>;
+    static_assert(NV == 0 || (TT == 16 && !PART), "narrow epilogues: 16-token tiles");
+    static_assert(C::NC >= 16 || !PART, "the partials mode stores 16-column chunks");
     static_assert(!(PART && FQ), "the partials mode reads codes from the standalone quantiser");
     extern __shared__ uint8_t smem_raw[];
     // Align by an offset from the __shared__ array itself: a pointer rebuilt from
@@ -530,8 +727,9 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
         // ============================================================ MMA issuers
         // With two issuers (Cfg::TWO_ISSUERS), issuer i owns the units u0 + i,
         // u0 + i + 2, ...: for those it waits for the stages, issues every MMA
-        // and commits the stages' buffers and the unit's accumulator slots; for
-        // the other issuer's units it only advances its ring positions.  Each
+        // and commits the stages' buffers and the unit's accumulator slots (from
+        // its own share of the slots); for the other issuer's units it only
+        // advances its stage ring positions.  Each
         // barrier hand-over costs a few hundred cycles, so splitting whole units
         // halves every issuer's share.  Otherwise issuer 0 owns every unit.
         const int me = warp - 1;
@@ -561,9 +759,10 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
                             // issuing thread ~250 cycles; unrolled ones ~17.)
 #pragma unroll
                             for (int s = 0; s < C::GPU / C::CG; ++s) {
-                                if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                                const int ps = C::acc_slot(sl, me);
+                                if (!mbar_wait(&bars->accempty[ps], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                                 tc_fence_after();
-                                const uint32_t d_slot = tbase + C::ACC0 + static_cast<uint32_t>(sl * C::CG * TT);
+                                const uint32_t d_slot = tbase + C::ACC0 + static_cast<uint32_t>(ps * C::CG * TT);
 #pragma unroll
                                 for (int gi = 0; gi < C::CG; ++gi) {
                                     const int gl = s * C::CG + gi;
@@ -576,19 +775,20 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
                                         tc_mma_i8_ts(d_slot + gi * TT, a_tmem + j * 64 + ks * 8, bd, idesc, t == 0 ? 0u : 1u);
                                     }
                                 }
-                                tc_commit(&bars->accfull[sl]);
-                                if (++sl == C::NACC) { sl = 0; slph ^= 1; }
+                                tc_commit(&bars->accfull[ps]);
+                                if (++sl == C::NRING) { sl = 0; slph ^= 1; }
                             }
                             if (!ok) break;
                         } else if (C::GK <= 256) {
                             // a ragged last unit: groups g0..g1, CG per accumulator slot
                             for (int g = g0; g < g1; ++g) {
                                 const int gl = g - g0, gi = gl % C::CG;
+                                const int ps = C::acc_slot(sl, me);
                                 if (gi == 0) {
-                                    if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                                    if (!mbar_wait(&bars->accempty[ps], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                                     tc_fence_after();
                                 }
-                                const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>((sl * C::CG + gi) * TT);
+                                const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>((ps * C::CG + gi) * TT);
                                 const int j = gl / C::GPK;                       // k-block within the stage
                                 const int s0 = (gl % C::GPK) * (C::GK / 32);     // first K step within it
 #pragma unroll
@@ -598,19 +798,20 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
                                     tc_mma_i8_ts(d_tmem, a_tmem + j * 64 + ks * 8, bd, idesc, t == 0 ? 0u : 1u);
                                 }
                                 if (gi == C::CG - 1 || g == g1 - 1) {
-                                    tc_commit(&bars->accfull[sl]);
-                                    if (++sl == C::NACC) { sl = 0; slph ^= 1; }
+                                    tc_commit(&bars->accfull[ps]);
+                                    if (++sl == C::NRING) { sl = 0; slph ^= 1; }
                                 }
                             }
                             if (!ok) break;
                         } else {
                             // one GK = 1024 group spread over several stages
                             const bool first_stage = kbs == kb0, last_stage = kbs + kn >= kb1;
+                            const int ps = C::acc_slot(sl, me);
                             if (first_stage) {
-                                if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
+                                if (!mbar_wait(&bars->accempty[ps], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
                                 tc_fence_after();
                             }
-                            const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>(sl * TT);
+                            const uint32_t d_tmem = tbase + C::ACC0 + static_cast<uint32_t>(ps * TT);
                             for (int j = 0; j < kn; ++j) {
 #pragma unroll
                                 for (int ks = 0; ks < 8; ++ks) {
@@ -620,26 +821,12 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
                                 }
                             }
                             if (last_stage) {
-                                tc_commit(&bars->accfull[sl]);
-                                if (++sl == C::NACC) { sl = 0; slph ^= 1; }
+                                tc_commit(&bars->accfull[ps]);
+                                if (++sl == C::NRING) { sl = 0; slph ^= 1; }
                             }
                         }
                         tc_commit(&bars->tempty[ab]);
                         tc_commit(&bars->aempty[sa]);
-                    } else {
-                        // The other issuer's stage: wait on its slots' phases as
-                        // well.  mbarrier waits match a phase by parity only, so
-                        // an issuer that skipped the other's phases could take a
-                        // phase from two rounds back for its own whenever a unit
-                        // uses as many slots as the ring holds.  The epilogue frees
-                        // slots in order, so these waits never hold the issuer
-                        // longer than its own next wait would.
-                        const int nslots = C::GK <= 256 ? (g1 - g0 + C::CG - 1) / C::CG : (kbs + kn >= kb1 ? 1 : 0);
-                        for (int i = 0; i < nslots; ++i) {
-                            if (!mbar_wait(&bars->accempty[sl], slph, abort_flag, p.status, kWMmaAccEmpty)) { ok = false; break; }
-                            if (++sl == C::NACC) { sl = 0; slph ^= 1; }
-                        }
-                        if (!ok) break;
                     }
                     if (++ab == C::NA) { ab = 0; abph ^= 1; }
                     if (++sa == C::S_A) { sa = 0; saph ^= 1; }
@@ -800,113 +987,8 @@ __global__ void __launch_bounds__(Cfg<TT, GK, ASYM, FQ>::THREADS, 1)
         }
     } else {
         if (C::SPLIT_REGS) regs_inc<C::REGS_EPI>();
-        // ============================================================ epilogue
-        const int ew = warp - kNumPreWarps;
-        const int quarter = warp & 3;
-        const int part = ew >> 2;
-        const int row = quarter * 32 + lane;
-        const int col0 = part * C::NC;
-        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        constexpr int NCH = C::NCH;
-
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
-            for (int b = 0; b < C::NACC; ++b) mbar_arrive(&bars->accempty[b]);
-        __syncwarp();
-
-        uint64_t acc2[C::NC / 2];
-#pragma unroll
-        for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
-        int sl = 0, slot = 0;
-        uint32_t aph = 0, slph = 0;
-        bool ok = true;
-        Unit un = unit_of(p, u0);
-        for (int u = u0; ok && u < u1; ++u, unit_next(p, un)) {
-            int g0, g1;
-            unit_groups<C>(p, un.ut, g0, g1);
-            if (!warp_wait(&bars->sfull[slot], slph, abort_flag, p.status, kWEpiSlot)) { ok = false; break; }
-            const uint8_t* wsb = slot_ws(slot);
-            const float* asb = slot_as(slot);
-            // one accumulator slot holds CG groups: all of this unit's, or one
-            for (int gs = g0; gs < g1; gs += C::CG) {
-                if (!warp_wait(&bars->accfull[sl], aph, abort_flag, p.status, kWEpiAccFull)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t t_slot = tbase + lane_off + C::ACC0 + static_cast<uint32_t>(sl * C::CG * TT + col0);
-                // this row's weight scale of each group in the slot, read once
-                float wsv[C::CG];
-                if (!PART) {
-#pragma unroll
-                    for (int gi = 0; gi < C::CG; ++gi) {
-                        const int gl = min(gs + gi, g1 - 1) - g0;
-                        wsv[gi] = ws_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(wsb)[gl * 128 + row])
-                                          : reinterpret_cast<const float*>(wsb)[gl * 128 + row];
-                        if (C::SYM16) wsv[gi] *= 0.0625f;   // the unpack carried weights as 16*w
-                    }
-                }
-                // Batches of BCH chunks, software-pipelined: the next batch's
-                // tcgen05.ld is in flight while this batch is rescaled.  With
-                // EARLY_RELEASE the slot goes back to the MMA as soon as its last
-                // batch is in registers, otherwise after the rescale.
-                R16 r[2][C::BCH];
-#pragma unroll
-                for (int q = 0; q < C::BCH; ++q)
-                    tc_ld16(t_slot + (q / NCH) * TT + 16 * (q % NCH), r[0][q].v);
-                tc_wait_ld();
-#pragma unroll
-                for (int q = 0; q < C::BCH; ++q) reg_fence16(r[0][q].v);
-#pragma unroll
-                for (int b = 0; b < C::NB; ++b) {
-                    if (b + 1 < C::NB) {
-#pragma unroll
-                        for (int q = 0; q < C::BCH; ++q) {
-                            const int c = (b + 1) * C::BCH + q;
-                            tc_ld16(t_slot + (c / NCH) * TT + 16 * (c % NCH), r[(b + 1) & 1][q].v);
-                        }
-                    } else if (C::EARLY_RELEASE) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&bars->accempty[sl]);
-                        __syncwarp();
-                    }
-#pragma unroll
-                    for (int q = 0; q < C::BCH; ++q) {
-                        const int c = b * C::BCH + q, gi = c / NCH, i = c % NCH;
-                        const int g = gs + gi;
-                        if (g >= g1) continue;
-                        const int gl = g - g0;           // group index within the unit's scale entry
-                        if (PART)
-                            store_partials<C::SYM16>(p, r[b & 1][q], g, un.tt * TT + col0 + 16 * i, un.wt * 128 + row);
-                        else
-                            rescale_chunk<C::NC>(acc2, i, r[b & 1][q], wsv[gi], asb + gl * TT + col0 + 16 * i);
-                    }
-                    if (b + 1 < C::NB) {
-                        tc_wait_ld();
-#pragma unroll
-                        for (int q = 0; q < C::BCH; ++q) reg_fence16(r[(b + 1) & 1][q].v);
-                    }
-                }
-                if (!C::EARLY_RELEASE) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&bars->accempty[sl]);
-                    __syncwarp();
-                }
-                if (++sl == C::NACC) { sl = 0; aph ^= 1; }
-            }
-            if (!ok) break;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->sempty[slot]);
-            __syncwarp();
-            if (++slot == C::DS) { slot = 0; slph ^= 1; }
-
-            // ---- end of this CTA's share of tile t: store or hand over ----
-            if (un.ut == p.units_per_tile - 1 || u == u1 - 1) {
-                if (!PART) flush_tile<C>(p, un, u0, u1, cta, row, col0, acc2);
-#pragma unroll
-                for (int j = 0; j < C::NC / 2; ++j) acc2[j] = 0ull;
-            }
-        }
+        epilogue_role<C, PART, NV == 0 ? C::NC : NV, PUSH>(p, bars, smem, tbase, abort_flag, ws_bf16, warp, lane, u0,
+                                                           u1, cta);
     }
 
     // ---------------------------------------------------------------- teardown
@@ -976,7 +1058,7 @@ __global__ void prepare_weights_kernel(const PrepareParams p)
 // still streaming.  A CTA after the first one of a split tile starts its range
 // inside the tile, so its part is in its first-tile slot (flush_tile's side 0);
 // the first CTA's part is there only when its range starts with the tile.
-template <int TT>
+template <int TT, bool PUSH>
 __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, const int nctas)
 {
     pdl_launch_dependents();
@@ -1018,7 +1100,7 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, 
 #pragma unroll
                 for (int j = 0; j < 16; ++j) sum[j] += v[q][j];
         }
-        if (p.push.world) {
+        if constexpr (PUSH) {
             if (n < p.N)
                 for (int r = 0; r < p.push.world; ++r) {
                     __nv_bfloat16* dst = push_slot(p.push, r);
@@ -1038,11 +1120,11 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, 
     }
 }
 
-template <int TT, int GK, bool ASYM, bool PART, bool FQ = false>
+template <int TT, int GK, bool ASYM, bool PART, bool FQ = false, int NV = 0, int EPI = 0, bool PUSH = false>
 cudaError_t launch_t(const GemmParams& p, int grid, cudaStream_t stream, bool pdl, int ws_bf16)
 {
-    using C = Cfg<TT, GK, ASYM, FQ>;
-    auto kern = w4a8_gemm_kernel<TT, GK, ASYM, PART, FQ>;
+    using C = Cfg<TT, GK, ASYM, FQ, EPI>;
+    auto kern = w4a8_gemm_kernel<TT, GK, ASYM, PART, FQ, NV, EPI, PUSH>;
     // The shared-memory opt-in is per device; set it once per device.
     static bool attr_done[64] = {};
     int dev = 0;
@@ -1086,6 +1168,11 @@ cudaError_t launch_gk(const GemmParams& p, const GemmConfig& c, int grid, cudaSt
         else
             return cudaErrorInvalidValue;
     }
+    if (p.push.world) {
+        // the fused all-reduce's own instantiations (standalone quantiser, full epilogue)
+        return c.asym ? launch_t<TT, GK, true, false, false, 0, 0, true>(p, grid, s, pdl, c.ws_bf16)
+                      : launch_t<TT, GK, false, false, false, 0, 0, true>(p, grid, s, pdl, c.ws_bf16);
+    }
     if (c.fq) {
         // fused quantisation exists for 16-token tiles and GK <= 256 (the host plans it so)
         if constexpr (TT == 16 && GK <= 256)
@@ -1093,6 +1180,17 @@ cudaError_t launch_gk(const GemmParams& p, const GemmConfig& c, int grid, cudaSt
                           : launch_t<TT, GK, false, false, true>(p, grid, s, pdl, c.ws_bf16);
         else
             return cudaErrorInvalidValue;
+    }
+    if constexpr (TT == 16) {
+        // a call of at most 4 or 8 tokens: the epilogue rescales only those columns
+        if (p.M <= 4)
+            return c.asym ? launch_t<TT, GK, true, false, false, 4>(p, grid, s, pdl, c.ws_bf16)
+                          : launch_t<TT, GK, false, false, false, 4>(p, grid, s, pdl, c.ws_bf16);
+        if (p.M <= 8)
+            return c.asym ? launch_t<TT, GK, true, false, false, 8>(p, grid, s, pdl, c.ws_bf16)
+                          : launch_t<TT, GK, false, false, false, 8>(p, grid, s, pdl, c.ws_bf16);
+        return c.asym ? launch_t<TT, GK, true, false, false, 8, 2>(p, grid, s, pdl, c.ws_bf16)
+                      : launch_t<TT, GK, false, false, false, 8, 2>(p, grid, s, pdl, c.ws_bf16);
     }
     return c.asym ? launch_t<TT, GK, true, false>(p, grid, s, pdl, c.ws_bf16)
                   : launch_t<TT, GK, false, false>(p, grid, s, pdl, c.ws_bf16);
@@ -1146,11 +1244,13 @@ cudaError_t launch_splitk_reduce(const GemmParams& p, int tt, int grid, cudaStre
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    const bool push = p.push.world != 0;
     switch (tt) {
-        case 16: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<16>, p, grid);
-        case 32: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<32>, p, grid);
-        case 64: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<64>, p, grid);
-        case 128: return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<128>, p, grid);
+        case 16: return cudaLaunchKernelEx(&cfg, push ? splitk_reduce_kernel<16, true> : splitk_reduce_kernel<16, false>, p, grid);
+        case 32: return cudaLaunchKernelEx(&cfg, push ? splitk_reduce_kernel<32, true> : splitk_reduce_kernel<32, false>, p, grid);
+        case 64: return cudaLaunchKernelEx(&cfg, push ? splitk_reduce_kernel<64, true> : splitk_reduce_kernel<64, false>, p, grid);
+        case 128:
+            return cudaLaunchKernelEx(&cfg, push ? splitk_reduce_kernel<128, true> : splitk_reduce_kernel<128, false>, p, grid);
         default: return cudaErrorInvalidValue;
     }
 }
