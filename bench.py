@@ -548,7 +548,7 @@ def kernels_per_call(M, N, K, sms, gk=GK):
     last = K - (G - 1) * gk
     kpad = (G - 1) * (-(-gk // 64) * 64) + -(-last // 64) * 64
     kb_total = -(-kpad // 256)
-    upt = -(-kb_total // (2 if tt <= 32 else 1)) if gk <= 256 else G
+    upt = -(-kb_total // (2 if tt <= 16 else 1)) if gk <= 256 else G
     units = -(-N // 128) * -(-M // tt) * upt
     grid = max(1, min(sms, units))
     split = any((c * units // grid) % upt for c in range(1, grid))

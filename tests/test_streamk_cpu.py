@@ -39,7 +39,7 @@ def plan(M, N, K, gk, sms=SMS):
     tt = 16 if M <= 16 else (32 if M <= 32 else (64 if M <= 64 else 128))
     n_wt, n_tt = cdiv(N, 128), cdiv(M, tt)
     kb_total = cdiv(kpad(K, gk), 256)
-    ks = 2 if tt <= 32 else 1
+    ks = 2 if tt <= 16 else 1
     upt = cdiv(kb_total, ks) if gk <= 256 else cdiv(K, gk)
     units = n_wt * n_tt * upt
     grid = max(1, min(sms, units))

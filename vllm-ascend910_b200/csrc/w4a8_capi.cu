@@ -111,9 +111,9 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms, int tt_cap 
     p.n_wt = static_cast<int>(cdiv(N, 128));
     p.n_tt = static_cast<int>(cdiv(M, p.tt));
     p.kb_total = static_cast<int>(cdiv(p.Kpad, 256));
-    // units per tile: stages of two k-blocks for token tiles <= 32 (GK <= 256),
-    // one k-block for larger tiles, one group for GK = 1024 (the kernel's Cfg)
-    const int ks = p.tt <= 32 ? 2 : 1;
+    // units per tile: stage_kblocks(tt) k-blocks (GK <= 256), one group for
+    // GK = 1024 (the kernel's Cfg)
+    const int ks = stage_kblocks(p.tt);
     p.upt = gk <= 256 ? static_cast<int>(cdiv(p.kb_total, ks)) : static_cast<int>(p.G);
     p.units = p.n_wt * p.n_tt * p.upt;
     p.grid = std::max(1, std::min(sms, p.units));
@@ -191,7 +191,7 @@ uint64_t g_map_clock = 0;
 std::mutex g_map_mutex;
 
 // Groups per GEMM unit (the scale / zero-point box height): the kernel's Cfg::GPU.
-int groups_per_unit(const Plan& pl) { return pl.gk <= 256 ? (pl.tt <= 32 ? 2 : 1) * (256 / pl.gk) : 1; }
+int groups_per_unit(const Plan& pl) { return pl.gk <= 256 ? stage_kblocks(pl.tt) * (256 / pl.gk) : 1; }
 
 bool encode_maps(const Plan& pl, const void* w_packed, const void* w_scale, int32_t ws_dtype, const void* w_zero,
                  CUtensorMap* m)

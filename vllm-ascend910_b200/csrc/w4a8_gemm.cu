@@ -61,9 +61,9 @@ struct Cfg {
     static constexpr bool FQ = FQ_;
     static_assert(!FQ || (TT == 16 && GK <= 256), "fused quantisation: 16-token tiles, GK <= 256");
     // Pipeline granularity.  Every hand-over between warps costs a few
-    // hundred cycles of mbarrier latency, so small token tiles move two
-    // k-blocks (32 KB of int4 weights) per stage.
-    static constexpr int KS = TT <= 32 ? 2 : 1;              // k-blocks per stage
+    // hundred cycles of mbarrier latency, so 16-token tiles move two k-blocks
+    // (32 KB of int4 weights) per stage.
+    static constexpr int KS = stage_kblocks(TT);             // k-blocks per stage
     static constexpr int GPK = GK <= 256 ? 256 / GK : 1;     // groups per k-block
     static constexpr int UKB = GK <= 256 ? KS : GK / 256;    // k-blocks per unit (max)
     static constexpr int GPU = GK <= 256 ? KS * GPK : 1;     // groups per unit (max)
@@ -75,11 +75,13 @@ struct Cfg {
     static constexpr int QWARP0 = kNumPreWarps + 4 * E;      // first quantiser warp
     static constexpr int THREADS = (kNumPreWarps + 4 * E + NQW) * 32;
     // TMEM: NA A buffers of KS x 64 columns (the stage's int8 weights), the
-    // rest for accumulator slots of CG groups x TT columns.  Tiles of 64 and
-    // 128 tokens keep two A buffers (128 columns) so their slots hold three
-    // units (measured: 64-token tiles 2-4 % faster than with four buffers).
+    // rest for accumulator slots of CG groups x TT columns.  Tiles of 32 to
+    // 128 tokens keep two A buffers (128 columns), so their slots hold three
+    // or more units (measured: 64-token tiles 2-4 % faster than with four
+    // buffers; 32-token tiles with one-k-block units 3 % faster over the
+    // four projections than with two-k-block units and two slots of slack).
     static constexpr int ABUF = KS * 64;
-    static constexpr int NA = (TT <= 32 ? 256 : 128) / ABUF;
+    static constexpr int NA = (TT <= 16 ? 256 : 128) / ABUF;
     static constexpr int ACC0 = NA * ABUF;
     static constexpr int ACC_COLS = 512 - ACC0;
     static constexpr int CG_FIT = ACC_COLS / (4 * TT);       // keeps >= 4 slots
@@ -113,7 +115,7 @@ struct Cfg {
     static constexpr int SL_AS = GPU * TT * 4;
     static constexpr int SLOT = r128(SL_WS) + r128(SL_AS);
     static constexpr int DS = FQ ? 6 : 8;
-    static constexpr int S_A = FQ ? 2 : (TT <= 16 ? 4 : (TT <= 32 ? 2 : (TT <= 64 ? 4 : 3)));
+    static constexpr int S_A = FQ ? 2 : (TT <= 64 ? 4 : 3);
     static constexpr int X_BOX = TT * 512;                   // one 2-D copy: TT rows x 256 bf16
     static constexpr int X_STAGE = FQ ? KS * X_BOX : 0;
     static constexpr int XS = FQ ? 2 : 0;

@@ -69,6 +69,11 @@ struct PushParams {
 };
 
 // The GEMM's view of one call.  Tensor maps are built on the host.
+// k-blocks (256 K positions) per pipeline stage and stream-K unit when
+// GK <= 256: two for 16-token tiles (32 KB of int4 weights per unit), one for
+// wider tiles.  The host plan and the kernel's Cfg both take it from here.
+__host__ __device__ constexpr int stage_kblocks(int tt) { return tt <= 16 ? 2 : 1; }
+
 struct alignas(64) GemmParams {
     // raw (reference-layout) weights, read with 2-D tensor copies
     CUtensorMap tm_w;    // packed int4 weights [N, Kpad/2] bytes, box {128 B, 128 rows}, SW128
