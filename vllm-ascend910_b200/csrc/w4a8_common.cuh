@@ -307,6 +307,16 @@ __host__ __device__ constexpr uint32_t idesc_i8(uint32_t M, uint32_t N)
 // ---------------------------------------------------------------- packed fp32 pairs
 // sm_100 executes two fp32 lanes per instruction on a 64-bit register pair.
 
+// The pair (lo, hi) as one 64-bit register pair, formed inside PTX with
+// mov.b64 {lo, hi}: the register allocator then places lo and hi in adjacent
+// registers instead of the shift-and-or a C++ 64-bit expression compiles to.
+__device__ __forceinline__ uint64_t pair2(float lo, float hi)
+{
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+
 __device__ __forceinline__ uint64_t pack2(float lo, float hi)
 {
     return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);

@@ -261,15 +261,15 @@ template <int NC>
 __device__ __forceinline__ void rescale_chunk(uint64_t (&acc2)[NC / 2], int i, const R16& r, float wsv,
                                               const float* asg)
 {
-    const uint64_t ws2 = pack2(wsv, wsv);
+    const uint64_t ws2 = pair2(wsv, wsv);
 #pragma unroll
     for (int j = 0; j < 16; j += 4) {
         const float4 a4 = *reinterpret_cast<const float4*>(asg + j);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const uint32_t r0 = r.v[j + 2 * h], r1 = r.v[j + 2 * h + 1];
-            const uint64_t f2 = pack2(__int2float_rn(static_cast<int>(r0)), __int2float_rn(static_cast<int>(r1)));
-            const uint64_t c2 = f2_mul(ws2, h == 0 ? pack2(a4.x, a4.y) : pack2(a4.z, a4.w));
+            const uint64_t f2 = pair2(__int2float_rn(static_cast<int>(r0)), __int2float_rn(static_cast<int>(r1)));
+            const uint64_t c2 = f2_mul(ws2, h == 0 ? pair2(a4.x, a4.y) : pair2(a4.z, a4.w));
             uint64_t& a = acc2[8 * i + j / 2 + h];
             a = f2_fma(f2, c2, a);
         }
@@ -280,15 +280,15 @@ __device__ __forceinline__ void rescale_chunk(uint64_t (&acc2)[NC / 2], int i, c
 template <int NC, int NV>
 __device__ __forceinline__ void rescale_cols(uint64_t (&acc2)[NC / 2], const uint32_t* r, float wsv, const float* asg)
 {
-    const uint64_t ws2 = pack2(wsv, wsv);
+    const uint64_t ws2 = pair2(wsv, wsv);
 #pragma unroll
     for (int j = 0; j < NV; j += 4) {
         const float4 a4 = *reinterpret_cast<const float4*>(asg + j);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const uint64_t f2 = pack2(__int2float_rn(static_cast<int>(r[j + 2 * h])),
+            const uint64_t f2 = pair2(__int2float_rn(static_cast<int>(r[j + 2 * h])),
                                       __int2float_rn(static_cast<int>(r[j + 2 * h + 1])));
-            const uint64_t c2 = f2_mul(ws2, h == 0 ? pack2(a4.x, a4.y) : pack2(a4.z, a4.w));
+            const uint64_t c2 = f2_mul(ws2, h == 0 ? pair2(a4.x, a4.y) : pair2(a4.z, a4.w));
             uint64_t& a = acc2[j / 2 + h];
             a = f2_fma(f2, c2, a);
         }
