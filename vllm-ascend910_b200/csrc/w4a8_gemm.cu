@@ -23,8 +23,10 @@
 //     slot holds one K-unit's groups when the token tile is small, else one
 //     group), so the MMA runs several groups ahead of the rescale instead of
 //     waiting for it.  A group's first MMA overwrites its region (no clear).
-//   * Epilogue warps: one batch of tcgen05.ld per slot, acc += P * (ws * as)
-//     with packed f32x2 arithmetic in registers, bf16 store at tile end.
+//   * Epilogue warps: tcgen05.ld of each slot's partials, acc += P * (ws * as)
+//     with packed f32x2 arithmetic in registers, bf16 store at tile end.  A
+//     16-token tile rescales only the token columns the call has (4 or 8 per
+//     thread at M <= 4 / 8; two warpgroups of 8 at M = 9..16).
 //   * Work split: stream-K over (tile, K-unit) so every SM gets the same number
 //     of weight bytes.  A tile split across CTAs leaves fp32 parts that a small
 //     fix-up kernel (chained by programmatic dependent launch) sums in CTA
