@@ -309,34 +309,11 @@ __host__ __device__ constexpr uint32_t idesc_i8(uint32_t M, uint32_t N)
 
 // The pair (lo, hi) as one 64-bit register pair, formed inside PTX with
 // mov.b64 {lo, hi}: the register allocator then places lo and hi in adjacent
-// registers instead of the shift-and-or a C++ 64-bit expression compiles to.
+// registers, with no shift-and-or of a C++ 64-bit expression to untangle.
 __device__ __forceinline__ uint64_t pair2(float lo, float hi)
 {
     uint64_t d;
     asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-    return d;
-}
-
-__device__ __forceinline__ uint64_t pack2(float lo, float hi)
-{
-    return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
-}
-
-__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi)
-{
-    return static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
-}
-
-__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi)
-{
-    lo = __uint_as_float(static_cast<uint32_t>(v));
-    hi = __uint_as_float(static_cast<uint32_t>(v >> 32));
-}
-
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b)
-{
-    uint64_t d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
 
