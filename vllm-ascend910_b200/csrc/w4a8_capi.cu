@@ -387,7 +387,7 @@ int check_weights(const void* w_packed, const void* w_scale, int32_t ws_dtype, c
 // contents are gone, and the next call looks it up and clears it again.  The
 // whole array is cleared on that first call per context, after which the
 // kernels leave the status word at zero unless a wait runs out.
-__device__ __align__(256) uint8_t g_fixed_scratch[W4A8_FIXED_SCRATCH_BYTES];
+static __device__ __align__(256) uint8_t g_fixed_scratch[W4A8_FIXED_SCRATCH_BYTES];
 uint8_t* g_fixed_ptr[kMaxDev];
 unsigned long long g_fixed_ctx[kMaxDev];   // cuCtxGetId of the context g_fixed_ptr belongs to
 std::mutex g_fixed_mutex;
