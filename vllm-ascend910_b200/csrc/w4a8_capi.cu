@@ -97,7 +97,7 @@ struct Plan {
 
 // tt_cap bounds the token tile (the debug partials mode runs 16-token tiles).
 // A smaller tile never needs more workspace than the tile chosen for M.
-Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms, int tt_cap = 128)
+Plan compute_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms, int tt_cap)
 {
     Plan p{};
     p.M = M;
@@ -128,6 +128,30 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms, int tt_cap 
     p.off_part = off;
     off += static_cast<size_t>(2) * p.grid * p.tt * 128 * 4;
     p.total = round_up(off, 1024);
+    return p;
+}
+
+// compute_plan behind a small per-thread cache: a serving loop calls the same
+// few shapes over and over, and the plan's split test walks every CTA.
+Plan make_plan(int64_t M, int64_t N, int64_t K, int32_t gk, int sms, int tt_cap = 128)
+{
+    struct Entry {
+        int64_t M, N, K;
+        int32_t gk;
+        int sms, tt_cap;
+        Plan plan;
+    };
+    constexpr int kEntries = 16;
+    thread_local Entry cache[kEntries];
+    thread_local int used = 0, next = 0;
+    for (int i = 0; i < used; ++i) {
+        const Entry& e = cache[i];
+        if (e.M == M && e.N == N && e.K == K && e.gk == gk && e.sms == sms && e.tt_cap == tt_cap) return e.plan;
+    }
+    const Plan p = compute_plan(M, N, K, gk, sms, tt_cap);
+    cache[next] = Entry{M, N, K, gk, sms, tt_cap, p};
+    next = (next + 1) % kEntries;
+    if (used < kEntries) ++used;
     return p;
 }
 

@@ -1116,12 +1116,12 @@ __global__ void __launch_bounds__(128) splitk_reduce_kernel(const GemmParams p, 
                         if (m < p.M) dst[static_cast<int64_t>(m) * p.N + n] = __float2bfloat16_rn(sum[j]);
                     }
                 }
-            return;
-        }
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int m = tt * TT + c0 + j;
-            if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
+            for (int j = 0; j < 16; ++j) {
+                const int m = tt * TT + c0 + j;
+                if (m < p.M && n < p.N) y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(sum[j]);
+            }
         }
     }
 }
